@@ -1,0 +1,202 @@
+/*
+ * nmsparse_b200.h -- C ABI of libnmsparse_b200.so, the B200 (sm_100a) N:M
+ * sparse GEMV decode path.
+ *
+ * Conventions
+ *   - All pointers are device pointers unless stated otherwise; all tensors
+ *     are dense and contiguous; fp16 means IEEE binary16.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Calls enqueue work and return without synchronizing.
+ *   - Every function returns an nms_status (0 = success).  On failure nothing
+ *     is launched and nms_last_error() returns a message for the calling
+ *     thread.  The Python layer maps NMS_ERR_VALUE -> ValueError,
+ *     NMS_ERR_TYPE -> TypeError, NMS_ERR_NOT_IMPLEMENTED ->
+ *     NotImplementedError and the others -> RuntimeError, the exception types
+ *     the reference raises for the same conditions (triton_spmv.py:245-283).
+ *
+ * Layouts (w = K*N/M compressed width, G = K/M groups, h = output rows)
+ *   mat_data  fp16 [w, h]   reference layout, element (j, r) at j*h + r
+ *                            (triton_spmv.py:10-13, src/spmv/nmsparse_linear.py:22-24)
+ *   mat_index u8   [G, N]   sorted in-group offsets shared by all rows
+ *                            (src/spmv/nmsparse_linear.py:22-26)
+ *   packed    fp16 [h, w_pad] row-major transpose of mat_data, rows zero
+ *                            padded to w_pad = nms_packed_row_stride(w)
+ */
+#ifndef NMSPARSE_B200_H_
+#define NMSPARSE_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NMS_ABI_VERSION 1
+
+enum nms_status {
+  NMS_OK = 0,
+  NMS_ERR_VALUE = -1,           /* bad shape, size, pointer or alignment   */
+  NMS_ERR_TYPE = -2,            /* unsupported dtype                       */
+  NMS_ERR_NOT_IMPLEMENTED = -3, /* valid request outside what is built     */
+  NMS_ERR_CUDA = -4,            /* CUDA runtime error                      */
+  NMS_ERR_DEVICE = -5           /* a kernel reported an error (see below)  */
+};
+
+int nms_abi_version(void);
+const char* nms_last_error(void);
+const char* nms_status_name(int status);
+/* Number of SMs of the current device (also checks it is an sm_100 part). */
+int nms_num_sms(int* out);
+/* Reads the device error word that kernels set instead of faulting or
+ * hanging (1 = bulk-copy wait timed out, 2 = attention position outside the
+ * KV cache; the kernel skipped its work).  Synchronizes the current device.  With
+ * clear != 0 the word is reset to 0. */
+int nms_device_error(int* code_out, int clear);
+
+/* ---------------------------------------------------------------------------
+ * Shared-mask N:M GEMV on the reference layout.
+ * Replaces nmsparse_spmv_forward_triton_ptx (triton_spmv.py:229-318) and the
+ * triton_ptx branch of the nmsparse::gemv op (src/spmv/nmsparse_op.py:82-96):
+ *   out[r] = sum_g sum_i mat_data[g*N + i, r] * vec[g*M + mat_index[g, i]]
+ * fp16 in, fp32 accumulation, fp16 out.  No zero-initialised fp32 scratch
+ * and no separate cast kernel: out is written once.
+ *   vec [K] fp16, mat_data [w, h] fp16 (32-byte aligned), mat_index [w/N, N],
+ *   out [h] fp16.  Requires h % 128 == 0, w % N == 0, K == (w/N)*M, M <= 256.
+ * ------------------------------------------------------------------------- */
+int nms_gemv_f16(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K,
+                 int64_t w, int64_t h, int32_t block_width, int32_t vec_width, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Packed layout (the re-laid-out packer; no reference counterpart: the
+ * reference streams mat_data[w, h] directly, triton_spmv.py:100-106).
+ * nms_pack_f16 / nms_unpack_f16 convert between mat_data[w, h] and
+ * packed[h, w_pad]; the round trip is bit-exact.
+ * ------------------------------------------------------------------------- */
+int64_t nms_packed_row_stride(int64_t w);
+int nms_pack_f16(const void* mat_data, void* packed, int64_t w, int64_t h, int64_t w_pad, void* stream);
+int nms_unpack_f16(const void* packed, void* mat_data, int64_t w, int64_t h, int64_t w_pad, void* stream);
+
+/* Same GEMV as nms_gemv_f16 on the packed layout (any h >= 1).  Used by
+ * NmSparseLinear.forward for single-token input
+ * (src/spmv/nmsparse_linear.py:62-66). */
+int nms_gemv_packed_f16(const void* vec, const void* packed, const void* mat_index, void* out, int64_t K,
+                        int64_t w, int64_t w_pad, int64_t h, int32_t block_width, int32_t vec_width,
+                        void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused decode launches (packed layout).  One launch covers several linears
+ * that read the same input vector:
+ *   NMS_EPI_STORE   segments' outputs concatenated: q/k/v
+ *                   (model.py:196-198,219 fused wqkv; HF q_proj/k_proj/v_proj)
+ *   NMS_EPI_SWIGLU  two segments (gate, up) with equal rows:
+ *                   out = silu(gate(x)) * up(x)        (model.py:255-256)
+ *   NMS_EPI_ARGMAX  dense (NMS_FLAG_DENSE) output head: logits and greedy
+ *                   token = argmax(logits), lowest index on ties
+ *                   (model.py:168-169, generate.py:46-63 with greedy choice)
+ * Prologue NMS_PRO_RESID_RMSNORM computes xin = fp16(x + x2) (x2 may be
+ * NULL), writes xin to resid_out (if not NULL) and feeds
+ * rmsnorm(xin) * norm_weight to the GEMV (model.py:185-188, 259-270).
+ * Each segment may carry its own mat_index (masks differ per linear,
+ * src/spmv/nmsparse_linear.py:118).
+ * ------------------------------------------------------------------------- */
+#define NMS_MAX_SEGMENTS 4
+#define NMS_EPI_STORE 0
+#define NMS_EPI_SWIGLU 1
+#define NMS_EPI_ARGMAX 2
+#define NMS_PRO_PLAIN 0
+#define NMS_PRO_RESID_RMSNORM 1
+#define NMS_FLAG_PDL 1   /* launch with programmatic dependent launch */
+#define NMS_FLAG_DENSE 2 /* dense rows: w == K, mat_index must be NULL */
+
+typedef struct nms_segment {
+  const void* packed;    /* [rows, w_pad] fp16, 32-byte aligned */
+  const void* mat_index; /* [w/N, N] u8, or NULL for dense      */
+  int64_t rows;
+} nms_segment;
+
+typedef struct nms_gemv_fused_args {
+  nms_segment seg[NMS_MAX_SEGMENTS];
+  int32_t nseg;
+  int32_t epilogue; /* NMS_EPI_* */
+  int32_t prologue; /* NMS_PRO_* */
+  int32_t flags;    /* NMS_FLAG_* */
+  int64_t K, w, w_pad;
+  int32_t block_width, vec_width; /* N, M (ignored when dense) */
+  const void* x;           /* [K] fp16 */
+  const void* x2;          /* [K] fp16 or NULL (prologue addend) */
+  const void* norm_weight; /* [K] fp16 (RMSNorm prologue) */
+  float eps;
+  void* resid_out; /* [K] fp16 or NULL */
+  void* out;       /* [sum rows] fp16 (STORE/ARGMAX) or [rows] (SWIGLU) */
+  /* argmax epilogue scratch: amax_capacity partials, a counter that must be
+   * zero before the first launch (the kernel resets it), the token output */
+  float* amax_val;
+  int32_t* amax_idx;
+  uint32_t* amax_counter;
+  int64_t* token_out;
+  int32_t amax_capacity;
+  int32_t grid;           /* CTAs (0 = two per SM) */
+  int32_t prefetch_bytes; /* per-CTA L2 prefetch before the dependency wait */
+} nms_gemv_fused_args;
+
+int nms_gemv_fused_f16(const nms_gemv_fused_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Single-token attention with KV-cache append (batch 1, head_dim 128).
+ * Replaces Attention.forward after the qkv projection (model.py:219-242:
+ * split, RoPE, KVCache.update, flex_attention/SDPA with GQA) and the HF
+ * Qwen3 attention with q_norm/k_norm (bench_qwen_3_32b_fp16_fixed_ptx.py:
+ * 331-355 via transformers).
+ * ------------------------------------------------------------------------- */
+#define NMS_ROPE_INTERLEAVED 0 /* gpt-fast pairs (2i, 2i+1), model.py:310-322 */
+#define NMS_ROPE_HALF 1        /* HF rotate_half pairs (i, i + D/2)          */
+
+typedef struct nms_attention_args {
+  const void* qkv;     /* [Hq*D + 2*Hkv*D] fp16: q | k | v of the new token */
+  void* k_cache;       /* [Hkv, S_max, D] fp16 */
+  void* v_cache;       /* [Hkv, S_max, D] fp16 */
+  const void* rope;    /* [S_max, D/2, 2] fp16 (cos, sin) */
+  const void* q_norm;  /* [D] fp16 or NULL */
+  const void* k_norm;  /* [D] fp16 or NULL */
+  const int64_t* pos;  /* device scalar: position of the new token, < S_max */
+  void* y;             /* [Hq*D] fp16 */
+  int32_t Hq, Hkv, D, S_max;
+  int32_t rope_style;
+  int32_t splits; /* CTAs per KV head, 1..16 (0 = automatic) */
+  float norm_eps;
+  float scale; /* usually 1/sqrt(D) */
+  int32_t flags; /* NMS_FLAG_PDL */
+} nms_attention_args;
+
+int nms_attention_decode_f16(const nms_attention_args* args, void* stream);
+
+/* x = table[token] (token read on the device).  Replaces tok_embeddings
+ * (model.py:164). */
+int nms_embedding_f16(const void* table, const int64_t* token, void* x, int64_t K, int64_t vocab, int32_t flags,
+                      void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Launch plans: a native executor for one decode step.  Launches are
+ * validated and frozen when added; nms_plan_launch replays a range of them
+ * on a stream with no per-launch validation, so a decode step costs one
+ * call from the host (or one CUDA-graph replay of that call).  Replaces the
+ * torch.compile + CUDAGraph capture of decode_one_token
+ * (benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:155-170).
+ * ------------------------------------------------------------------------- */
+typedef struct nms_plan nms_plan;
+
+int nms_plan_create(nms_plan** out);
+int nms_plan_destroy(nms_plan* plan);
+int nms_plan_add_gemv(nms_plan* plan, const nms_gemv_fused_args* args);
+int nms_plan_add_attention(nms_plan* plan, const nms_attention_args* args);
+int nms_plan_add_embedding(nms_plan* plan, const void* table, const int64_t* token, void* x, int64_t K,
+                           int64_t vocab, int32_t flags);
+int nms_plan_size(const nms_plan* plan, int32_t* out);
+/* Launch records [begin, end) on `stream`. */
+int nms_plan_launch(const nms_plan* plan, int32_t begin, int32_t end, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NMSPARSE_B200_H_ */

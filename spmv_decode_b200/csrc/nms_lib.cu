@@ -1,0 +1,609 @@
+// libnmsparse_b200: C-ABI entry points for the B200 N:M sparse GEMV decode path.
+//
+// One translation unit: every kernel header is included here, so file-scope
+// __device__ state (the device error word) exists once per loaded library.
+// The ABI uses plain pointers, 64-bit sizes and an opaque stream handle
+// (cudaStream_t passed as void*; nullptr = legacy default stream).  Every
+// entry point validates its arguments, never aborts, and returns an
+// nms_status code; nms_last_error() gives the message of the calling
+// thread's last failure.
+//
+// Each launch is first turned into a frozen LaunchRec (kernel choice,
+// parameters, grid, shared memory, launch attributes).  The direct entry
+// points launch the record immediately; the plan API stores records and
+// replays them (nms_plan_launch), which is the decode-step executor.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/nmsparse_b200.h"
+#include "nms_common.cuh"
+#include "nms_decode.cuh"
+#include "nms_gemv.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int fail_cuda(cudaError_t e, const char* what) {
+  return fail(NMS_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+constexpr int kMaxDevices = 64;
+constexpr int kGemvCtasPerSm = 2;  // packed GEMV: two 512-thread CTAs per SM
+
+struct DeviceInfo {
+  bool ready = false;
+  int num_sms = 0;
+  size_t max_smem_optin = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+// Per-device one-time setup: SM count, opt-in shared memory, and the
+// function attributes of every kernel instantiation.
+int device_info(const DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NMS_ERR_VALUE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    int major = 0, minor = 0, sms = 0, smem = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (major != 10 || minor != 0)
+      return fail(NMS_ERR_NOT_IMPLEMENTED,
+                  "libnmsparse_b200 is built for sm_100a (B200); device %d is sm_%d%d", dev, major, minor);
+    d.num_sms = sms;
+    d.max_smem_optin = (size_t)smem;
+    const void* dyn_smem_kernels[] = {
+        (const void*)nms::gemv_packed_kernel<32>, (const void*)nms::gemv_packed_kernel<16>,
+        (const void*)nms::gemv_packed_kernel<8>,  (const void*)nms::gemv_packed_kernel<4>,
+        (const void*)nms::gemv_ref_kernel<8>,
+    };
+    size_t static_max = 0;
+    for (const void* k : dyn_smem_kernels) {
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, k);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncGetAttributes");
+      if (fa.sharedSizeBytes > static_max) static_max = fa.sharedSizeBytes;
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem - (int)fa.sharedSizeBytes);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+    }
+    // Dynamic shared memory available to every kernel that takes it.
+    d.max_smem_optin = (size_t)smem - static_max;
+    e = cudaFuncSetAttribute((const void*)nms::attention_decode_kernel,
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(NonPortableClusterSizeAllowed)");
+    d.ready = true;
+  }
+  *out = &d;
+  return NMS_OK;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                      dim3 cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = cluster.x;
+    attrs[na].val.clusterDim.y = cluster.y;
+    attrs[na].val.clusterDim.z = cluster.z;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+struct EmbedParams {
+  const __half* table;
+  const int64_t* token;
+  __half* x;
+  int K;
+  int64_t vocab;
+};
+
+// A frozen, validated launch.
+struct LaunchRec {
+  enum Kind { kGemvPacked, kGemvRef, kAttention, kEmbedding, kPack, kUnpack } kind;
+  int lanes = 0;  // gemv_packed_kernel template argument
+  nms::GemvParams gp;
+  nms::GemvRefParams rp;
+  nms::AttnParams ap;
+  EmbedParams ep;
+  struct {
+    const __half* src;
+    __half* dst;
+    int w, h, w_pad;
+  } pk;
+  dim3 grid, block, cluster{1, 1, 1};
+  size_t smem = 0;
+  bool pdl = false;
+};
+
+int launch_rec(const LaunchRec& r, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  switch (r.kind) {
+    case LaunchRec::kGemvPacked:
+      switch (r.lanes) {
+        case 32: e = launch_ex(nms::gemv_packed_kernel<32>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp); break;
+        case 16: e = launch_ex(nms::gemv_packed_kernel<16>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp); break;
+        case 8: e = launch_ex(nms::gemv_packed_kernel<8>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp); break;
+        default: e = launch_ex(nms::gemv_packed_kernel<4>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp); break;
+      }
+      break;
+    case LaunchRec::kGemvRef:
+      e = launch_ex(nms::gemv_ref_kernel<8>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.rp);
+      break;
+    case LaunchRec::kAttention:
+      e = launch_ex(nms::attention_decode_kernel, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.ap);
+      break;
+    case LaunchRec::kEmbedding:
+      e = launch_ex(nms::embedding_kernel, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.ep.table, r.ep.token,
+                    r.ep.x, r.ep.K, r.ep.vocab);
+      break;
+    case LaunchRec::kPack:
+      e = launch_ex(nms::pack_kernel, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.pk.src, r.pk.dst, r.pk.w,
+                    r.pk.h, r.pk.w_pad);
+      break;
+    case LaunchRec::kUnpack:
+      e = launch_ex(nms::unpack_kernel, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.pk.src, r.pk.dst, r.pk.w,
+                    r.pk.h, r.pk.w_pad);
+      break;
+  }
+  if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
+  return NMS_OK;
+}
+
+int pick_lanes_per_row(int64_t w_pad) {
+  for (int L = 32; L >= 4; L >>= 1)
+    if (w_pad % (16 * L) == 0) return L;
+  return 0;
+}
+
+// Shared validation of the N:M shape parameters (reference checks:
+// triton_spmv.py:255-283, src/spmv/nmsparse_linear.py:39).
+int check_nm(int64_t K, int64_t w, int32_t n, int32_t m) {
+  if (n < 1 || m < 1) return fail(NMS_ERR_VALUE, "block_width=%d and vec_width=%d must be positive", n, m);
+  if (n > m) return fail(NMS_ERR_VALUE, "block_width=%d must not exceed vec_width=%d", n, m);
+  if (m > 256) return fail(NMS_ERR_VALUE, "vec_width=%d exceeds the uint8 in-group offset range", m);
+  if (w <= 0 || K <= 0) return fail(NMS_ERR_VALUE, "w=%lld and K=%lld must be positive", (long long)w, (long long)K);
+  if (w % n != 0) return fail(NMS_ERR_VALUE, "w=%lld must be divisible by N=%d", (long long)w, n);
+  if ((w / n) * (int64_t)m != K)
+    return fail(NMS_ERR_VALUE, "vector length K=%lld != (w/N)*M = %lld", (long long)K, (long long)((w / n) * m));
+  if (K > (1 << 24)) return fail(NMS_ERR_VALUE, "K=%lld too large", (long long)K);
+  return NMS_OK;
+}
+
+// Build the record of a packed-layout GEMV launch (all fused variants).
+int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
+  if (a == nullptr) return fail(NMS_ERR_VALUE, "args is null");
+  if (a->nseg < 1 || a->nseg > NMS_MAX_SEGMENTS) return fail(NMS_ERR_VALUE, "nseg=%d out of range", a->nseg);
+  if (!a->x || !a->out) return fail(NMS_ERR_VALUE, "null x or out pointer");
+  const bool dense = (a->flags & NMS_FLAG_DENSE) != 0;
+  int rc;
+  if (dense) {
+    if (a->w != a->K) return fail(NMS_ERR_VALUE, "dense launch needs w == K (w=%lld, K=%lld)", (long long)a->w, (long long)a->K);
+    if (a->K <= 0 || a->K > (1 << 24)) return fail(NMS_ERR_VALUE, "bad K=%lld", (long long)a->K);
+  } else {
+    rc = check_nm(a->K, a->w, a->block_width, a->vec_width);
+    if (rc) return rc;
+  }
+  for (int i = 0; i < a->nseg; ++i) {
+    const nms_segment& s = a->seg[i];
+    if (!dense && s.mat_index == nullptr) return fail(NMS_ERR_VALUE, "segment %d: null mat_index", i);
+    if (dense && s.mat_index != nullptr) return fail(NMS_ERR_VALUE, "dense launch must not pass mat_index");
+    if (s.packed == nullptr) return fail(NMS_ERR_VALUE, "segment %d: null weight pointer", i);
+    if (!aligned(s.packed, 32)) return fail(NMS_ERR_VALUE, "segment %d: packed weights must be 32-byte aligned", i);
+    if (s.rows <= 0) return fail(NMS_ERR_VALUE, "segment %d: rows must be positive", i);
+  }
+  int mode = nms::kModeConcat, epi = nms::kEpiStore, pro = nms::kProPlain;
+  if (a->epilogue == NMS_EPI_SWIGLU) {
+    mode = nms::kModePaired;
+    epi = nms::kEpiSwiGLU;
+  } else if (a->epilogue == NMS_EPI_ARGMAX) {
+    epi = nms::kEpiArgmax;
+    if (!a->amax_val || !a->amax_idx || !a->amax_counter || !a->token_out)
+      return fail(NMS_ERR_VALUE, "argmax epilogue needs amax_val, amax_idx, amax_counter and token_out");
+  } else if (a->epilogue != NMS_EPI_STORE) {
+    return fail(NMS_ERR_VALUE, "unknown epilogue %d", a->epilogue);
+  }
+  if (a->prologue == NMS_PRO_RESID_RMSNORM) {
+    pro = nms::kProResidNorm;
+    if (!a->norm_weight) return fail(NMS_ERR_VALUE, "rmsnorm prologue needs norm_weight");
+  } else if (a->prologue != NMS_PRO_PLAIN) {
+    return fail(NMS_ERR_VALUE, "unknown prologue %d", a->prologue);
+  }
+  if (a->prefetch_bytes < 0) return fail(NMS_ERR_VALUE, "prefetch_bytes must be >= 0");
+
+  const DeviceInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  const int64_t K = a->K, w = a->w, w_pad = a->w_pad;
+  const int L = pick_lanes_per_row(w_pad);
+  if (L == 0) return fail(NMS_ERR_VALUE, "packed row stride w_pad=%lld must be a multiple of 64", (long long)w_pad);
+  if (w_pad < w) return fail(NMS_ERR_VALUE, "w_pad=%lld < w=%lld", (long long)w_pad, (long long)w);
+  const int RG = 32 / L;
+
+  nms::GemvParams& p = rec->gp;
+  memset(&p, 0, sizeof(p));
+  int64_t rows_total = 0;
+  const bool paired = (mode == nms::kModePaired);
+  for (int i = 0; i < a->nseg; ++i) {
+    const nms_segment& s = a->seg[i];
+    p.seg[i].w = static_cast<const __half*>(s.packed);
+    p.seg[i].idx = static_cast<const uint8_t*>(s.mat_index);
+    p.seg[i].rows = (int32_t)s.rows;
+    p.seg[i].row_start = paired ? 0 : (int32_t)rows_total;
+    if (!paired) rows_total += s.rows;
+  }
+  if (paired) {
+    if (a->nseg != 2 || a->seg[0].rows != a->seg[1].rows)
+      return fail(NMS_ERR_VALUE, "SwiGLU epilogue needs two segments (gate, up) with equal rows");
+    rows_total = a->seg[0].rows;
+  }
+  if (rows_total > (1 << 30)) return fail(NMS_ERR_VALUE, "too many rows");
+  p.nseg = a->nseg;
+  p.mode = mode;
+  p.prologue = pro;
+  p.epilogue = epi;
+  p.K = (int32_t)K;
+  p.n = dense ? 1 : a->block_width;
+  p.m = dense ? 1 : a->vec_width;
+  p.w = (int32_t)w;
+  p.w_pad = (int32_t)w_pad;
+  p.rows_total = (int32_t)rows_total;
+  p.row_groups = (int32_t)((rows_total + RG - 1) / RG);
+  p.prefetch_bytes = a->prefetch_bytes;
+  p.x = static_cast<const __half*>(a->x);
+  p.x2 = static_cast<const __half*>(a->x2);
+  p.norm_w = static_cast<const __half*>(a->norm_weight);
+  p.eps = a->eps;
+  p.resid_out = static_cast<__half*>(a->resid_out);
+  p.out = static_cast<__half*>(a->out);
+  p.amax_val = a->amax_val;
+  p.amax_idx = a->amax_idx;
+  p.amax_counter = a->amax_counter;
+  p.token_out = a->token_out;
+
+  int grid = a->grid > 0 ? a->grid : dev->num_sms * kGemvCtasPerSm;
+  if (grid > p.row_groups) grid = p.row_groups;
+  if (grid < 1) grid = 1;
+  if (epi == nms::kEpiArgmax && grid > a->amax_capacity)
+    return fail(NMS_ERR_VALUE, "argmax scratch holds %d partials, the launch needs %d", a->amax_capacity, grid);
+  const int nsegx = paired ? 2 : a->nseg;
+  const int max_vrows = (paired ? 2 : 1) * ((p.row_groups + grid - 1) / grid) * RG;
+  const size_t smem = nms::gemv_smem_bytes((int)K, (int)w, (int)w_pad, nsegx, max_vrows);
+  if (smem > dev->max_smem_optin)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "K=%lld, w_pad=%lld, %d masks need %zu bytes of shared memory (limit %zu)",
+                (long long)K, (long long)w_pad, nsegx, smem, dev->max_smem_optin);
+  rec->kind = LaunchRec::kGemvPacked;
+  rec->lanes = L;
+  rec->grid = dim3(grid);
+  rec->block = dim3(nms::kGemvThreads);
+  rec->smem = smem;
+  rec->pdl = (a->flags & NMS_FLAG_PDL) != 0;
+  return NMS_OK;
+}
+
+int prepare_attention(const nms_attention_args* a, LaunchRec* rec) {
+  if (a == nullptr) return fail(NMS_ERR_VALUE, "args is null");
+  if (!a->qkv || !a->k_cache || !a->v_cache || !a->rope || !a->pos || !a->y)
+    return fail(NMS_ERR_VALUE, "null pointer argument");
+  if (a->D != nms::kAttnD) return fail(NMS_ERR_NOT_IMPLEMENTED, "head_dim=%d (only %d is built)", a->D, nms::kAttnD);
+  if (a->Hkv < 1 || a->Hq < a->Hkv || a->Hq % a->Hkv != 0)
+    return fail(NMS_ERR_VALUE, "Hq=%d must be a positive multiple of Hkv=%d", a->Hq, a->Hkv);
+  if (a->Hq / a->Hkv > nms::kAttnMaxGroup)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "GQA group %d > %d", a->Hq / a->Hkv, nms::kAttnMaxGroup);
+  if (a->S_max < 1) return fail(NMS_ERR_VALUE, "S_max must be positive");
+  if (a->rope_style != NMS_ROPE_INTERLEAVED && a->rope_style != NMS_ROPE_HALF)
+    return fail(NMS_ERR_VALUE, "unknown rope_style %d", a->rope_style);
+  if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16)) return fail(NMS_ERR_VALUE, "KV cache must be 16-byte aligned");
+  const DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  int splits = a->splits;
+  if (splits <= 0) {
+    splits = (2 * dev->num_sms + a->Hkv - 1) / a->Hkv;
+    if (splits > 8) splits = 8;
+    if (splits < 1) splits = 1;
+  }
+  if (splits > 16) return fail(NMS_ERR_VALUE, "splits=%d > 16", splits);
+  nms::AttnParams& p = rec->ap;
+  p.qkv = static_cast<const __half*>(a->qkv);
+  p.k_cache = static_cast<__half*>(a->k_cache);
+  p.v_cache = static_cast<__half*>(a->v_cache);
+  p.rope = static_cast<const __half*>(a->rope);
+  p.q_norm = static_cast<const __half*>(a->q_norm);
+  p.k_norm = static_cast<const __half*>(a->k_norm);
+  p.pos = a->pos;
+  p.y = static_cast<__half*>(a->y);
+  p.norm_eps = a->norm_eps;
+  p.scale = a->scale;
+  p.Hq = a->Hq;
+  p.Hkv = a->Hkv;
+  p.S_max = a->S_max;
+  p.rope_style = a->rope_style;
+  p.splits = splits;
+  rec->kind = LaunchRec::kAttention;
+  rec->grid = dim3(splits, a->Hkv);
+  rec->block = dim3(nms::kAttnThreads);
+  rec->cluster = dim3(splits, 1, 1);
+  rec->smem = 0;
+  rec->pdl = (a->flags & NMS_FLAG_PDL) != 0;
+  return NMS_OK;
+}
+
+int prepare_embedding(const void* table, const int64_t* token, void* x, int64_t K, int64_t vocab, int32_t flags,
+                      LaunchRec* rec) {
+  if (!table || !token || !x) return fail(NMS_ERR_VALUE, "null pointer argument");
+  if (K <= 0 || K > (1 << 24) || vocab <= 0) return fail(NMS_ERR_VALUE, "bad sizes K=%lld vocab=%lld", (long long)K, (long long)vocab);
+  rec->kind = LaunchRec::kEmbedding;
+  rec->ep = EmbedParams{static_cast<const __half*>(table), token, static_cast<__half*>(x), (int)K, vocab};
+  rec->grid = dim3((unsigned)((K + 255) / 256 < 64 ? (K + 255) / 256 : 64));
+  rec->block = dim3(256);
+  rec->smem = 0;
+  rec->pdl = (flags & NMS_FLAG_PDL) != 0;
+  return NMS_OK;
+}
+
+}  // namespace
+
+struct nms_plan {
+  std::vector<LaunchRec> recs;
+};
+
+extern "C" {
+
+int nms_abi_version(void) { return NMS_ABI_VERSION; }
+
+const char* nms_last_error(void) { return g_last_error.c_str(); }
+
+const char* nms_status_name(int status) {
+  switch (status) {
+    case NMS_OK: return "NMS_OK";
+    case NMS_ERR_VALUE: return "NMS_ERR_VALUE";
+    case NMS_ERR_TYPE: return "NMS_ERR_TYPE";
+    case NMS_ERR_NOT_IMPLEMENTED: return "NMS_ERR_NOT_IMPLEMENTED";
+    case NMS_ERR_CUDA: return "NMS_ERR_CUDA";
+    case NMS_ERR_DEVICE: return "NMS_ERR_DEVICE";
+    default: return "NMS_ERR_UNKNOWN";
+  }
+}
+
+int nms_num_sms(int* out) {
+  if (out == nullptr) return fail(NMS_ERR_VALUE, "out is null");
+  const DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  *out = dev->num_sms;
+  return NMS_OK;
+}
+
+int nms_device_error(int* code_out, int clear) {
+  if (code_out == nullptr) return fail(NMS_ERR_VALUE, "code_out is null");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, nms::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMemcpyFromSymbol(device error)");
+  *code_out = v;
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(nms::g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMemcpyToSymbol(device error)");
+  }
+  return NMS_OK;
+}
+
+int nms_gemv_f16(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K, int64_t w,
+                 int64_t h, int32_t block_width, int32_t vec_width, void* stream) {
+  if (!vec || !mat_data || !mat_index || !out) return fail(NMS_ERR_VALUE, "null pointer argument");
+  int rc = check_nm(K, w, block_width, vec_width);
+  if (rc) return rc;
+  if (h <= 0 || h % 128 != 0) return fail(NMS_ERR_VALUE, "h must be divisible by 128 (got %lld)", (long long)h);
+  if (h > (1 << 28)) return fail(NMS_ERR_VALUE, "h=%lld too large", (long long)h);
+  if (!aligned(mat_data, 32)) return fail(NMS_ERR_VALUE, "mat_data must be 32-byte aligned");
+  const DeviceInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  constexpr int LR = 8, RB = 16 * LR;
+  const int64_t nblocks = h / RB;
+  int cs = (int)((2 * dev->num_sms + nblocks - 1) / nblocks);
+  if (cs > 8) cs = 8;
+  const int64_t max_cs_by_width = w / 256 > 0 ? w / 256 : 1;
+  if (cs > max_cs_by_width) cs = (int)max_cs_by_width;
+  if (cs < 1) cs = 1;
+  const int64_t jchunk = (w + cs - 1) / cs;
+  LaunchRec rec;
+  nms::GemvRefParams& p = rec.rp;
+  p.vec = static_cast<const __half*>(vec);
+  p.mat_data = static_cast<const __half*>(mat_data);
+  p.mat_index = static_cast<const uint8_t*>(mat_index);
+  p.out = static_cast<__half*>(out);
+  p.K = (int32_t)K;
+  p.w = (int32_t)w;
+  p.h = (int32_t)h;
+  p.n = block_width;
+  p.m = vec_width;
+  p.jchunk = (int32_t)jchunk;
+  p.cs = cs;
+  rec.kind = LaunchRec::kGemvRef;
+  rec.smem = nms::align_up_sz((size_t)jchunk * 2, 16) + (size_t)(nms::kGemvWarps + 1) * RB * 4;
+  if (rec.smem > dev->max_smem_optin)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "w=%lld too large for one CTA slice", (long long)w);
+  rec.grid = dim3((unsigned)nblocks, (unsigned)cs);
+  rec.block = dim3(nms::kGemvThreads);
+  rec.cluster = dim3(1, (unsigned)cs, 1);
+  return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int64_t nms_packed_row_stride(int64_t w) {
+  if (w <= 0) return 0;
+  return (w + 63) / 64 * 64;
+}
+
+static int pack_common(const void* src, void* dst, int64_t w, int64_t h, int64_t w_pad, void* stream, bool pack) {
+  if (!src || !dst) return fail(NMS_ERR_VALUE, "null pointer argument");
+  if (w <= 0 || h <= 0 || w_pad < w)
+    return fail(NMS_ERR_VALUE, "bad sizes w=%lld h=%lld w_pad=%lld", (long long)w, (long long)h, (long long)w_pad);
+  if (w_pad > (1 << 26) || h > (1 << 26)) return fail(NMS_ERR_VALUE, "sizes too large");
+  LaunchRec rec;
+  rec.kind = pack ? LaunchRec::kPack : LaunchRec::kUnpack;
+  rec.pk.src = static_cast<const __half*>(src);
+  rec.pk.dst = static_cast<__half*>(dst);
+  rec.pk.w = (int)w;
+  rec.pk.h = (int)h;
+  rec.pk.w_pad = (int)w_pad;
+  rec.grid = dim3((unsigned)(((pack ? w_pad : w) + 31) / 32), (unsigned)((h + 31) / 32));
+  rec.block = dim3(32, 8);
+  return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int nms_pack_f16(const void* mat_data, void* packed, int64_t w, int64_t h, int64_t w_pad, void* stream) {
+  return pack_common(mat_data, packed, w, h, w_pad, stream, true);
+}
+
+int nms_unpack_f16(const void* packed, void* mat_data, int64_t w, int64_t h, int64_t w_pad, void* stream) {
+  return pack_common(packed, mat_data, w, h, w_pad, stream, false);
+}
+
+int nms_gemv_packed_f16(const void* vec, const void* packed, const void* mat_index, void* out, int64_t K, int64_t w,
+                        int64_t w_pad, int64_t h, int32_t block_width, int32_t vec_width, void* stream) {
+  if (!vec || !packed || !mat_index || !out) return fail(NMS_ERR_VALUE, "null pointer argument");
+  if (h <= 0) return fail(NMS_ERR_VALUE, "h must be positive");
+  nms_gemv_fused_args a;
+  memset(&a, 0, sizeof(a));
+  a.seg[0].packed = packed;
+  a.seg[0].mat_index = mat_index;
+  a.seg[0].rows = h;
+  a.nseg = 1;
+  a.epilogue = NMS_EPI_STORE;
+  a.prologue = NMS_PRO_PLAIN;
+  a.K = K;
+  a.w = w;
+  a.w_pad = w_pad;
+  a.block_width = block_width;
+  a.vec_width = vec_width;
+  a.x = vec;
+  a.out = out;
+  LaunchRec rec;
+  int rc = prepare_gemv(&a, &rec);
+  if (rc) return rc;
+  return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int nms_gemv_fused_f16(const nms_gemv_fused_args* args, void* stream) {
+  LaunchRec rec;
+  int rc = prepare_gemv(args, &rec);
+  if (rc) return rc;
+  return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int nms_attention_decode_f16(const nms_attention_args* args, void* stream) {
+  LaunchRec rec;
+  int rc = prepare_attention(args, &rec);
+  if (rc) return rc;
+  return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int nms_embedding_f16(const void* table, const int64_t* token, void* x, int64_t K, int64_t vocab, int32_t flags,
+                      void* stream) {
+  LaunchRec rec;
+  int rc = prepare_embedding(table, token, x, K, vocab, flags, &rec);
+  if (rc) return rc;
+  return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int nms_plan_create(nms_plan** out) {
+  if (out == nullptr) return fail(NMS_ERR_VALUE, "out is null");
+  *out = new (std::nothrow) nms_plan();
+  if (*out == nullptr) return fail(NMS_ERR_CUDA, "out of host memory");
+  return NMS_OK;
+}
+
+int nms_plan_destroy(nms_plan* plan) {
+  delete plan;
+  return NMS_OK;
+}
+
+int nms_plan_add_gemv(nms_plan* plan, const nms_gemv_fused_args* args) {
+  if (plan == nullptr) return fail(NMS_ERR_VALUE, "plan is null");
+  LaunchRec rec;
+  int rc = prepare_gemv(args, &rec);
+  if (rc) return rc;
+  plan->recs.push_back(rec);
+  return NMS_OK;
+}
+
+int nms_plan_add_attention(nms_plan* plan, const nms_attention_args* args) {
+  if (plan == nullptr) return fail(NMS_ERR_VALUE, "plan is null");
+  LaunchRec rec;
+  int rc = prepare_attention(args, &rec);
+  if (rc) return rc;
+  plan->recs.push_back(rec);
+  return NMS_OK;
+}
+
+int nms_plan_add_embedding(nms_plan* plan, const void* table, const int64_t* token, void* x, int64_t K, int64_t vocab,
+                           int32_t flags) {
+  if (plan == nullptr) return fail(NMS_ERR_VALUE, "plan is null");
+  LaunchRec rec;
+  int rc = prepare_embedding(table, token, x, K, vocab, flags, &rec);
+  if (rc) return rc;
+  plan->recs.push_back(rec);
+  return NMS_OK;
+}
+
+int nms_plan_size(const nms_plan* plan, int32_t* out) {
+  if (plan == nullptr || out == nullptr) return fail(NMS_ERR_VALUE, "null argument");
+  *out = (int32_t)plan->recs.size();
+  return NMS_OK;
+}
+
+int nms_plan_launch(const nms_plan* plan, int32_t begin, int32_t end, void* stream) {
+  if (plan == nullptr) return fail(NMS_ERR_VALUE, "plan is null");
+  const int32_t n = (int32_t)plan->recs.size();
+  if (begin < 0 || end > n || begin > end) return fail(NMS_ERR_VALUE, "range [%d, %d) outside plan of %d", begin, end, n);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int32_t i = begin; i < end; ++i) {
+    int rc = launch_rec(plan->recs[i], st);
+    if (rc) return rc;
+  }
+  return NMS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,242 @@
+"""NmSparseLinear and swap_to_nmsparse on the B200 packed layout.
+
+Mirrors src/spmv/nmsparse_linear.py of the reference:
+
+* ``make_sparse(K, N, M, seed, device)`` restates the reference packer
+  ``_make_sparse`` (src/spmv/nmsparse_linear.py:14-33) in its shared-mask
+  form (NM_KERNEL=triton_ptx): the same seeded CPU generator, the same draw
+  order, so ``mat_data`` [w, N] and ``mat_index`` [K/M, M/2] are bit-exact
+  with the reference's.
+* ``NmSparseLinear(N, K, M, seed, device, dense_weight=None)`` has the
+  reference constructor, attributes ``h, w, block_width, vec_width``,
+  buffers ``mat_data`` and ``mat_index`` and forward rule (single token ->
+  sparse GEMV, otherwise ``F.linear`` with the dense weight,
+  :55-68).  The difference is storage: ``mat_data`` holds the packed layout
+  [h, w_pad] (row-major transpose, 16-byte aligned rows) that the sm_100a
+  kernel streams; ``reference_mat_data()`` returns the reference [w, h]
+  layout, and reference state dicts load unchanged (they are repacked).
+* ``swap_to_nmsparse(model, M, device, seed=0, block_devices=None)`` replaces
+  the same linears in the same order with the same seeds (:71-144).
+
+Environment variables ``NM_DECODE_ONLY`` and ``NM_WEIGHT_CPU`` keep the
+reference meaning (:7-8).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import nmsparse_op  # noqa: F401  (registers torch.ops.nmsparse.*)
+from .nmsparse_op import pack, packed_row_stride, unpack
+
+DECODE_ONLY = os.environ.get("NM_DECODE_ONLY", "0") == "1"
+WEIGHT_CPU = os.environ.get("NM_WEIGHT_CPU", "0") == "1" or DECODE_ONLY
+
+LAYOUT_PACKED = 1
+
+
+def make_sparse(K: int, N: int, M: int, seed: int, device="cpu"):
+    """Synthetic shared-mask N:M weights, bit-exact with the reference packer.
+
+    Returns ``(mat_data [w, N] fp16, mat_index [K/M, M/2] uint8, w, nnz)`` on
+    ``device``; 50% sparsity (nnz = M/2) as in the reference
+    (src/spmv/nmsparse_linear.py:14-33, shared-mask branch :22-26).
+    """
+    nnz = M // 2
+    nb = K // M
+    w = nb * nnz
+    g = torch.Generator().manual_seed(seed)
+    mat_data = (torch.randn(w, N, generator=g, dtype=torch.float32) / (K ** 0.5)).to(torch.float16)
+    mat_index = torch.empty(nb, nnz, dtype=torch.uint8)
+    for bank in range(nb):
+        mat_index[bank] = torch.randperm(M, generator=g)[:nnz].sort().values.to(torch.uint8)
+    if str(device) != "cpu":
+        mat_data = mat_data.to(device)
+        mat_index = mat_index.to(device)
+    return mat_data, mat_index, w, nnz
+
+
+def make_sparse_device(K: int, N: int, M: int, seed: int, device, std: float | None = None):
+    """Synthetic shared-mask weights drawn directly on a CUDA device and
+    packed there: same distribution as ``make_sparse`` (randn/sqrt(K), or
+    N(0, std) when ``std`` is given; uniform random sorted in-group masks) but
+    not the same numbers.  Used to build multi-GB benchmark models in seconds.
+
+    Returns ``(packed [N, w_pad] fp16, mat_index [K/M, M/2] uint8, w, nnz)``.
+    """
+    nnz = M // 2
+    nb = K // M
+    w = nb * nnz
+    gen = torch.Generator(device=device).manual_seed(seed)
+    w_pad = packed_row_stride(w)
+    packed = torch.zeros((N, w_pad), dtype=torch.float16, device=device)
+    scale = std if std is not None else 1.0 / (K ** 0.5)
+    # Draw in row blocks to bound the fp32 temporary.
+    rows_per = max(1, (1 << 26) // max(w, 1))
+    for r0 in range(0, N, rows_per):
+        r1 = min(N, r0 + rows_per)
+        blk = torch.randn((r1 - r0, w), generator=gen, dtype=torch.float32, device=device)
+        packed[r0:r1, :w] = (blk * scale).to(torch.float16)
+    keys = torch.rand((nb, M), generator=gen, device=device)
+    mat_index = keys.argsort(dim=1)[:, :nnz].sort(dim=1).values.to(torch.uint8).contiguous()
+    return packed, mat_index, w, nnz
+
+
+def masked_dense(mat_data: torch.Tensor, mat_index: torch.Tensor, K: int, M: int) -> torch.Tensor:
+    """Dense [h, K] weight with the kept values scattered back to their
+    columns (the reference microbench's ``weight_sparse``,
+    microbench_triton_torchmv.py:145-164).  Host/device agnostic."""
+    w, h = mat_data.shape
+    nb, nnz = mat_index.shape
+    cols = (torch.arange(nb, device=mat_index.device).unsqueeze(1) * M + mat_index.long()).reshape(-1)
+    dense = torch.zeros((h, K), dtype=mat_data.dtype, device=mat_data.device)
+    dense[:, cols.to(mat_data.device)] = mat_data.t()
+    return dense
+
+
+class NmSparseLinear(nn.Module):
+    """Shared-mask 50% N:M sparse linear (reference: src/spmv/nmsparse_linear.py:36-68)."""
+
+    def __init__(self, N, K, M, seed, device, dense_weight=None, *, init: str = "reference"):
+        super().__init__()
+        assert K % M == 0 and N % 128 == 0, (K, N, M)
+        self._weight_cpu = None
+        self.weight = None
+        if dense_weight is not None:
+            if WEIGHT_CPU:
+                self._weight_cpu = dense_weight.detach().cpu()
+                del dense_weight
+                if str(device) != "cpu" and torch.cuda.is_available():
+                    torch.cuda.empty_cache()
+            else:
+                self.weight = dense_weight
+        if init == "reference":
+            md, mi, w, nnz = make_sparse(K, N, M, seed, device)
+            packed = pack(md)
+            del md
+        elif init == "device":
+            packed, mi, w, nnz = make_sparse_device(K, N, M, seed, device)
+        elif init == "empty":
+            nnz = M // 2
+            w = (K // M) * nnz
+            packed = torch.zeros((N, packed_row_stride(w)), dtype=torch.float16, device=device)
+            mi = torch.zeros((K // M, nnz), dtype=torch.uint8, device=device)
+        else:
+            raise ValueError(f"unknown init={init!r}")
+        self.register_buffer("mat_data", packed)
+        self.register_buffer("mat_index", mi)
+        self.register_buffer("mat_layout", torch.tensor([LAYOUT_PACKED], dtype=torch.uint8, device=packed.device))
+        self.h, self.w, self.block_width, self.vec_width = N, w, nnz, M
+        self.in_features, self.out_features = K, N
+
+    @property
+    def w_pad(self) -> int:
+        return int(self.mat_data.shape[-1])
+
+    def reference_mat_data(self) -> torch.Tensor:
+        """The kept values in the reference layout [w, h] (bit-exact)."""
+        return unpack(self.mat_data, self.w)
+
+    def dense_masked_weight(self) -> torch.Tensor:
+        """[h, K] dense weight holding the kept values (zeros elsewhere)."""
+        return masked_dense(self.reference_mat_data(), self.mat_index, self.in_features, self.vec_width)
+
+    def _prefill_weight(self, device):
+        if self.weight is not None:
+            return self.weight
+        if self._weight_cpu is None:
+            raise RuntimeError("prefill requires dense weight")
+        return self._weight_cpu.to(device)
+
+    def forward(self, x):
+        if x.shape[-2] == 1:
+            return torch.ops.nmsparse.gemv_packed(
+                x, self.mat_data, self.mat_index,
+                self.w, self.h, self.block_width, self.vec_width,
+            )
+        return F.linear(x, self._prefill_weight(x.device))
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
+                              unexpected_keys, error_msgs):
+        # A reference state dict has mat_data in [w, h] and no layout marker.
+        key_d, key_l = prefix + "mat_data", prefix + "mat_layout"
+        if key_d in state_dict and key_l not in state_dict:
+            md = state_dict[key_d]
+            if tuple(md.shape) == (self.w, self.h):
+                state_dict[key_d] = pack(md.to(torch.float16), self.w_pad)
+                state_dict[key_l] = torch.tensor([LAYOUT_PACKED], dtype=torch.uint8)
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,
+                                      unexpected_keys, error_msgs)
+
+    def extra_repr(self) -> str:
+        return (f"in={self.in_features}, out={self.h}, {self.block_width}:{self.vec_width}, "
+                f"w={self.w}, w_pad={self.w_pad}")
+
+
+# Block layouts swap_to_nmsparse knows (reference :83-91): gpt-fast fused
+# attention (wqkv, wo) and MLP (w1, w3, w2); HF decoder blocks
+# (q/k/v/o_proj, gate/up/down_proj).
+_ATTENTION_LAYOUTS = (
+    ("attention", ("wqkv", "wo")),
+    ("self_attn", ("q_proj", "k_proj", "v_proj", "o_proj")),
+)
+
+_MLP_LAYOUTS = (
+    ("feed_forward", ("w1", "w3", "w2")),
+    ("mlp", ("gate_proj", "up_proj", "down_proj")),
+)
+
+
+def _resolve_layout(blk, layouts, kind):
+    for submodule_attr, linear_names in layouts:
+        submodule = getattr(blk, submodule_attr, None)
+        if submodule is not None:
+            return submodule, linear_names
+    known = ", ".join(f".{attr}" for attr, _ in layouts)
+    raise AttributeError(
+        f"decoder block {type(blk).__name__} has none of the known "
+        f"{kind} sub-modules ({known}); swap_to_nmsparse does not "
+        f"recognize this block's layout."
+    )
+
+
+def _swap_linears(submodule, linear_names, M, device, seed, cnt, init):
+    for name in linear_names:
+        old = getattr(submodule, name)
+        if isinstance(old, NmSparseLinear):
+            N, K = old.h, old.in_features
+        else:
+            N, K = old.weight.shape
+        dense_weight = None if (DECODE_ONLY or isinstance(old, NmSparseLinear)) else old.weight
+        del old
+        if torch.cuda.is_available():
+            torch.cuda.empty_cache()
+        setattr(submodule, name, NmSparseLinear(N, K, M, seed + cnt, device, dense_weight=dense_weight, init=init))
+        cnt += 1
+    return cnt
+
+
+def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str = "reference"):
+    """Replace every decoder block's attention and MLP linears with
+    NmSparseLinear (reference: src/spmv/nmsparse_linear.py:124-144).
+
+    Linear number ``cnt`` (in block order, attention then MLP, names in layout
+    order) gets seed ``seed + cnt``.  ``block_devices`` optionally gives one
+    device per block.  Returns the number of linears swapped.
+    ``init="device"`` draws the weights on the GPU instead (same
+    distribution, different numbers, much faster for multi-GB models).
+    """
+    cnt = 0
+    for i, blk in enumerate(model.layers):
+        blk_device = device
+        if block_devices is not None:
+            d = block_devices[i]
+            blk_device = d if isinstance(d, str) else f"cuda:{d}"
+        attn, attn_names = _resolve_layout(blk, _ATTENTION_LAYOUTS, "attention")
+        cnt = _swap_linears(attn, attn_names, M, blk_device, seed, cnt, init)
+        mlp, mlp_names = _resolve_layout(blk, _MLP_LAYOUTS, "feed-forward")
+        cnt = _swap_linears(mlp, mlp_names, M, blk_device, seed, cnt, init)
+    return cnt
