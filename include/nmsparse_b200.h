@@ -137,6 +137,14 @@ typedef struct nms_gemv_fused_args {
   int32_t amax_capacity;
   int32_t grid;           /* CTAs (0 = two per SM) */
   int32_t prefetch_bytes; /* per-CTA L2 prefetch before the dependency wait */
+  /* argmax generation hooks (each may be NULL): also write the token to
+   * next_token; if pos is set, write token_history[*pos] = token (when
+   * *pos < history_len) and then increment *pos.  Lets a captured decode
+   * step feed itself (generate.py:93-119 decode_n_tokens loop). */
+  int64_t* next_token;
+  int64_t* token_history;
+  int64_t* pos;
+  int64_t history_len;
 } nms_gemv_fused_args;
 
 int nms_gemv_fused_f16(const nms_gemv_fused_args* args, void* stream);

@@ -91,6 +91,10 @@ class NmsGemvFusedArgs(ctypes.Structure):
         ("amax_capacity", c_i32),
         ("grid", c_i32),
         ("prefetch_bytes", c_i32),
+        ("next_token", c_void_p),
+        ("token_history", c_void_p),
+        ("pos", c_void_p),
+        ("history_len", c_i64),
     ]
 
 

@@ -71,6 +71,11 @@ struct GemvParams {
   int32_t* amax_idx;     // [gridDim.x]
   uint32_t* amax_counter;  // zero before the first launch; reset by the last CTA
   int64_t* token_out;
+  // Generation hooks of the argmax epilogue (each optional):
+  int64_t* next_token;     // also write the token here (next step's input id)
+  int64_t* token_history;  // history[*pos] = token
+  int64_t* pos;            // position counter, incremented after the above
+  int64_t history_len;     // entries in token_history
 };
 
 // Position of compressed element j inside the permuted shared-memory copy of
@@ -235,6 +240,12 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
           }
         }
         *p.token_out = (int64_t)fi;
+        if (p.next_token != nullptr) *p.next_token = (int64_t)fi;
+        if (p.pos != nullptr) {
+          const int64_t cur = *p.pos;
+          if (p.token_history != nullptr && cur >= 0 && cur < p.history_len) p.token_history[cur] = (int64_t)fi;
+          *p.pos = cur + 1;
+        }
         *p.amax_counter = 0u;
       }
     }

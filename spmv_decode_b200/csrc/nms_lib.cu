@@ -300,6 +300,12 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
   p.amax_idx = a->amax_idx;
   p.amax_counter = a->amax_counter;
   p.token_out = a->token_out;
+  p.next_token = a->next_token;
+  p.token_history = a->token_history;
+  p.pos = a->pos;
+  p.history_len = a->history_len;
+  if (epi != nms::kEpiArgmax && (a->next_token || a->token_history || a->pos))
+    return fail(NMS_ERR_VALUE, "generation hooks need the argmax epilogue");
 
   int grid = a->grid > 0 ? a->grid : dev->num_sms * kGemvCtasPerSm;
   if (grid > p.row_groups) grid = p.row_groups;

@@ -1,0 +1,331 @@
+"""Fused batch-1 decode step on sm_100a: the engine behind decode_one_token.
+
+A ``DecodeEngine`` takes a ``Transformer`` whose linears are
+``NmSparseLinear`` (after ``swap_to_nmsparse``) or dense ``nn.Linear``, and
+freezes one decode step into a native launch plan (libnmsparse_b200
+``nms_plan_*``), replayed by a CUDA graph.  Per layer:
+
+  1. q/k/v GEMV (one launch; fused wqkv or three masks) with the residual
+     add + RMSNorm prologue                  model.py:185-186, 215-219
+  2. attention: q/k RMSNorm, RoPE, KV append, split-KV softmax(QK^T)V
+                                             model.py:221-242
+  3. o-projection GEMV                       model.py:244
+  4. gate/up GEMV with the residual + RMSNorm prologue and SwiGLU epilogue
+                                             model.py:187, 255-256
+  5. down-projection GEMV                    model.py:256
+and finally the residual + final RMSNorm + dense output head with a greedy
+argmax epilogue (model.py:168-169; generate.py:46-63 with greedy choice).
+The token embedding gather starts the step (model.py:164).  Every kernel is
+launched with programmatic dependent launch, so a kernel's weight stream
+starts while its predecessor finishes.
+
+Under tensor parallelism (``tp.TensorParallel``) each rank owns a column
+shard of q/k/v and gate/up and a row shard of o/down; the plan is cut after
+the o and down projections where an all-reduce of the partial sums runs.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Callable, List, Optional
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from .model import Transformer, precompute_rope_table
+from .nmsparse_linear import NmSparseLinear
+
+ARGMAX_CAPACITY = 2048
+
+
+def _linear_segment(lin) -> dict:
+    """Segment description (packed weights, mask, rows, shape) of a linear."""
+    if isinstance(lin, NmSparseLinear):
+        return dict(packed=lin.mat_data, idx=lin.mat_index, rows=lin.h, K=lin.in_features, w=lin.w,
+                    w_pad=lin.w_pad, n=lin.block_width, m=lin.vec_width, dense=False)
+    if isinstance(lin, nn.Linear) or hasattr(lin, "weight"):
+        wt = lin.weight
+        if wt.dtype != torch.float16 or not wt.is_contiguous():
+            raise TypeError("dense linears must hold contiguous float16 weights")
+        rows, K = wt.shape
+        return dict(packed=wt, idx=None, rows=rows, K=K, w=K, w_pad=K, n=1, m=1, dense=True)
+    raise TypeError(f"unsupported linear {type(lin).__name__}")
+
+
+class DecodeEngine:
+    """Batch-1 decode state + native plan for one model on one device."""
+
+    def __init__(self, model: Transformer, max_seq_length: int, *, pdl: bool = True, prefetch_bytes: int = 0,
+                 attn_splits: int = 0, history_len: int = 0,
+                 allreduce: Optional[Callable[[torch.Tensor], None]] = None, tp_rank: int = 0, tp_size: int = 1,
+                 local_heads: Optional[tuple] = None):
+        c = model.config
+        self.config = c
+        self.model = model
+        dev = model.tok_embeddings.weight.device
+        if dev.type != "cuda":
+            raise ValueError("DecodeEngine needs the model on a CUDA device")
+        self.device = dev
+        self.pdl = pdl
+        self.prefetch_bytes = int(prefetch_bytes)
+        self.allreduce = allreduce
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        Hq, Hkv = local_heads if local_heads is not None else (c.n_head, c.n_local_heads)
+        self.Hq, self.Hkv, self.D = Hq, Hkv, c.head_dim
+        self.max_seq_length = int(max_seq_length)
+        S = self.max_seq_length
+        f16 = dict(device=dev, dtype=torch.float16)
+        i64 = dict(device=dev, dtype=torch.int64)
+        dim = c.dim
+        qkv_rows = (Hq + 2 * Hkv) * c.head_dim
+        ffn0 = model.layers[0].ffn
+        inter_local = _linear_segment(getattr(ffn0, "w1", None) or ffn0.gate_proj)["rows"]
+
+        with torch.cuda.device(dev):
+            # Device scalars driving the step.
+            self.token_in = torch.zeros(1, **i64)
+            self.token_out = torch.zeros(1, **i64)
+            self.pos = torch.zeros(1, **i64)
+            self.history = torch.zeros(max(1, history_len), **i64)
+            # Activations (one token).
+            self.x_emb = torch.zeros(dim, **f16)
+            self.x_buf = torch.zeros(dim, **f16)  # residual stream after attention input
+            self.h_buf = torch.zeros(dim, **f16)  # residual stream after MLP input
+            self.qkv = torch.zeros(qkv_rows, **f16)
+            self.y_attn = torch.zeros(Hq * c.head_dim, **f16)
+            self.y_o = torch.zeros(dim, **f16)
+            self.act = torch.zeros(inter_local, **f16)
+            self.y_down = torch.zeros(dim, **f16)
+            head_w = model.output_weight
+            self.vocab_local = head_w.shape[0]
+            self.logits = torch.zeros(self.vocab_local, **f16)
+            self.amax_val = torch.zeros(ARGMAX_CAPACITY, device=dev, dtype=torch.float32)
+            self.amax_idx = torch.zeros(ARGMAX_CAPACITY, device=dev, dtype=torch.int32)
+            self.amax_counter = torch.zeros(1, device=dev, dtype=torch.int32)
+            # KV cache [L, Hkv, S, D] and RoPE table [S, D/2, 2].
+            self.k_cache = torch.zeros((c.n_layer, Hkv, S, c.head_dim), **f16)
+            self.v_cache = torch.zeros((c.n_layer, Hkv, S, c.head_dim), **f16)
+            self.rope = precompute_rope_table(S, c.head_dim, c.rope_base, torch.float16, c.rope_scaling,
+                                              c.rope_style).to(dev)
+            # fp16 copies of small parameters the kernels read.
+            self._keep: List[torch.Tensor] = []
+            self._plan = ctypes.c_void_p()
+            _lib.check(_lib.lib().nms_plan_create(ctypes.byref(self._plan)), "nms_plan_create")
+            self.cut_points: List[int] = []  # plan indices after which an all-reduce runs
+            self._build(model, attn_splits)
+
+    # ------------------------------------------------------------------ build
+    def _h(self, t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+        if t is None:
+            return None
+        t = t.detach().to(device=self.device, dtype=torch.float16).contiguous()
+        self._keep.append(t)
+        return t
+
+    def _flags(self, dense: bool = False) -> int:
+        return (_lib.NMS_FLAG_PDL if self.pdl else 0) | (_lib.NMS_FLAG_DENSE if dense else 0)
+
+    def _add_gemv(self, linears, *, x, out, x2=None, norm=None, eps=0.0, resid_out=None, swiglu=False,
+                  argmax=False, advance=False):
+        segs = [_linear_segment(l) for l in linears]
+        s0 = segs[0]
+        for s in segs[1:]:
+            if (s["K"], s["w"], s["w_pad"], s["n"], s["m"], s["dense"]) != (s0["K"], s0["w"], s0["w_pad"], s0["n"],
+                                                                          s0["m"], s0["dense"]):
+                raise ValueError("fused segments must share K, N:M pattern and packed stride")
+        a = _lib.NmsGemvFusedArgs()
+        for i, s in enumerate(segs):
+            a.seg[i].packed = s["packed"].data_ptr()
+            a.seg[i].mat_index = None if s["idx"] is None else s["idx"].data_ptr()
+            a.seg[i].rows = s["rows"]
+        a.nseg = len(segs)
+        a.epilogue = _lib.NMS_EPI_SWIGLU if swiglu else (_lib.NMS_EPI_ARGMAX if argmax else _lib.NMS_EPI_STORE)
+        a.prologue = _lib.NMS_PRO_RESID_RMSNORM if norm is not None else _lib.NMS_PRO_PLAIN
+        a.flags = self._flags(s0["dense"])
+        a.K, a.w, a.w_pad = s0["K"], s0["w"], s0["w_pad"]
+        a.block_width, a.vec_width = s0["n"], s0["m"]
+        a.x = x.data_ptr()
+        a.x2 = None if x2 is None else x2.data_ptr()
+        a.norm_weight = None if norm is None else norm.data_ptr()
+        a.eps = float(eps)
+        a.resid_out = None if resid_out is None else resid_out.data_ptr()
+        a.out = out.data_ptr()
+        a.prefetch_bytes = self.prefetch_bytes
+        if argmax:
+            a.amax_val = self.amax_val.data_ptr()
+            a.amax_idx = self.amax_idx.data_ptr()
+            a.amax_counter = self.amax_counter.data_ptr()
+            a.token_out = self.token_out.data_ptr()
+            a.amax_capacity = ARGMAX_CAPACITY
+            if advance:
+                a.next_token = self.token_in.data_ptr()
+                a.pos = self.pos.data_ptr()
+                a.token_history = self.history.data_ptr()
+                a.history_len = self.history.numel()
+        _lib.check(_lib.lib().nms_plan_add_gemv(self._plan, ctypes.byref(a)), "nms_plan_add_gemv")
+
+    def _build(self, model: Transformer, attn_splits: int):
+        c = self.config
+        L = _lib.lib()
+        emb = model.tok_embeddings.weight
+        if emb.dtype != torch.float16:
+            raise TypeError("model must be float16 (the reference decode path is fp16)")
+        self.emb = emb
+        _lib.check(L.nms_plan_add_embedding(self._plan, emb.data_ptr(), self.token_in.data_ptr(),
+                                            self.x_emb.data_ptr(), c.dim, emb.shape[0], self._flags()),
+                   "nms_plan_add_embedding")
+        for li, blk in enumerate(model.layers):
+            attn, ffn = blk.attn, blk.ffn
+            qkv_lins = [attn.wqkv] if c.attn_layout == "fused" else [attn.q_proj, attn.k_proj, attn.v_proj]
+            self._add_gemv(qkv_lins, x=self.x_emb if li == 0 else self.h_buf, x2=None if li == 0 else self.y_down,
+                           norm=self._h(blk.norm1.weight), eps=blk.norm1.eps, resid_out=self.x_buf, out=self.qkv)
+            aa = _lib.NmsAttentionArgs()
+            aa.qkv = self.qkv.data_ptr()
+            aa.k_cache = self.k_cache[li].data_ptr()
+            aa.v_cache = self.v_cache[li].data_ptr()
+            aa.rope = self.rope.data_ptr()
+            qn = self._h(attn.q_norm.weight) if getattr(attn, "q_norm", None) is not None else None
+            kn = self._h(attn.k_norm.weight) if getattr(attn, "k_norm", None) is not None else None
+            aa.q_norm = None if qn is None else qn.data_ptr()
+            aa.k_norm = None if kn is None else kn.data_ptr()
+            aa.pos = self.pos.data_ptr()
+            aa.y = self.y_attn.data_ptr()
+            aa.Hq, aa.Hkv, aa.D, aa.S_max = self.Hq, self.Hkv, c.head_dim, self.max_seq_length
+            aa.rope_style = _lib.NMS_ROPE_INTERLEAVED if c.rope_style == "interleaved" else _lib.NMS_ROPE_HALF
+            aa.splits = attn_splits
+            aa.norm_eps = float(attn.q_norm.eps) if qn is not None else 0.0
+            aa.scale = 1.0 / math.sqrt(c.head_dim)
+            aa.flags = self._flags()
+            _lib.check(L.nms_plan_add_attention(self._plan, ctypes.byref(aa)), "nms_plan_add_attention")
+            o_lin = attn.wo if c.attn_layout == "fused" else attn.o_proj
+            self._add_gemv([o_lin], x=self.y_attn, out=self.y_o)
+            self.cut_points.append(self.size())
+            gate, up, down = ((ffn.w1, ffn.w3, ffn.w2) if c.attn_layout == "fused"
+                              else (ffn.gate_proj, ffn.up_proj, ffn.down_proj))
+            self._add_gemv([gate, up], x=self.x_buf, x2=self.y_o, norm=self._h(blk.norm2.weight), eps=blk.norm2.eps,
+                           resid_out=self.h_buf, out=self.act, swiglu=True)
+            self._add_gemv([down], x=self.act, out=self.y_down)
+            self.cut_points.append(self.size())
+        self._head_index = self.size()
+        self._final_norm = self._h(model.norm.weight)
+        self._head_args = dict(x=self.h_buf, x2=self.y_down, norm=self._final_norm, eps=model.norm.eps,
+                               out=self.logits, argmax=True)
+        head = _HeadLinear(model.output_weight)
+        self._add_gemv([head], advance=False, **self._head_args)
+        self._add_gemv([head], advance=True, **self._head_args)  # variant used by generate()
+        self._plan_len = self._head_index + 1
+
+    def size(self) -> int:
+        n = ctypes.c_int32()
+        _lib.check(_lib.lib().nms_plan_size(self._plan, ctypes.byref(n)))
+        return int(n.value)
+
+    # ------------------------------------------------------------------- run
+    def _launch(self, begin: int, end: int, stream) -> None:
+        if end > begin:
+            _lib.check(_lib.lib().nms_plan_launch(self._plan, begin, end, stream.cuda_stream), "nms_plan_launch")
+
+    def step(self, advance: bool = False, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Enqueue one decode step: reads token_in and pos on the device,
+        writes logits and token_out (and with ``advance`` also token_in,
+        history[pos] and pos += 1)."""
+        stream = stream or torch.cuda.current_stream(self.device)
+        begin = 0
+        if self.allreduce is not None:
+            # Cut points alternate: after the o-projection (partial y_o) and
+            # after the down-projection (partial y_down) of every layer.
+            for i, cut in enumerate(self.cut_points):
+                self._launch(begin, cut, stream)
+                self.allreduce(self.y_o if i % 2 == 0 else self.y_down)
+                begin = cut
+        head = self._head_index + (1 if advance else 0)
+        self._launch(begin, self._head_index, stream)
+        self._launch(head, head + 1, stream)
+
+    def reset(self) -> None:
+        self.k_cache.zero_()
+        self.v_cache.zero_()
+        self.pos.zero_()
+        self.token_in.zero_()
+        self.history.zero_()
+
+    def fill_synthetic_cache(self, ctx: int, std: float = 0.02, seed: int = 0) -> None:
+        """Reference fixed-context protocol: KV cache ~ N(0, std), position ctx
+        (bench_llama_3_8b_fp16_fixed_ptx.py:145-152)."""
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        for t in (self.k_cache, self.v_cache):
+            t.normal_(0.0, std, generator=g)
+        self.pos.fill_(ctx)
+
+    def capture(self, advance: bool = False, warmup: int = 3) -> torch.cuda.CUDAGraph:
+        """CUDA graph of one decode step (side-stream warm-up, then capture)."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        pos0 = self.pos.clone()
+        tok0 = self.token_in.clone()
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.step(advance=advance, stream=s)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.pos.copy_(pos0)
+        self.token_in.copy_(tok0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.step(advance=advance, stream=s)
+        torch.cuda.synchronize(self.device)
+        return g
+
+    def close(self) -> None:
+        if self._plan:
+            _lib.lib().nms_plan_destroy(self._plan)
+            self._plan = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _HeadLinear:
+    """Dense output head adapter (tied or untied weight)."""
+
+    def __init__(self, weight: torch.Tensor):
+        self.weight = weight
+
+
+def smoke_step(dev: torch.device) -> None:
+    """Tiny fused decode step on ``dev`` checked against the CPU oracle (used
+    by __graft_entry__.smoke)."""
+    from .model import ModelArgs
+    from .nmsparse_linear import swap_to_nmsparse
+
+    cfg = ModelArgs(block_size=64, vocab_size=512, n_layer=2, n_head=2, dim=256, intermediate_size=512,
+                    n_local_heads=1)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Transformer(cfg)
+    with torch.no_grad():
+        model.tok_embeddings.weight.normal_(0, 0.02)
+        model.output.weight.normal_(0, 0.02)
+    model = model.to(torch.float16)
+    swap_to_nmsparse(model, 32, dev, seed=3)
+    eng = DecodeEngine(model, 32, history_len=32)
+    eng.token_in.fill_(7)
+    eng.pos.fill_(0)
+    eng.step()
+    torch.cuda.synchronize(dev)
+    from oracle.decode_oracle import OracleModel
+
+    om = OracleModel.from_transformer(model)
+    ref = om.step(7, 0)
+    got = eng.logits.float().cpu()
+    err = (got - ref.float()).abs().max().item()
+    scale = ref.float().abs().max().item()
+    if not (err <= 2e-2 * max(scale, 1e-3)):
+        raise AssertionError(f"smoke decode step mismatch: max abs err {err}, logit scale {scale}")
+    if int(eng.token_out.item()) != int(torch.argmax(eng.logits).item()):
+        raise AssertionError("smoke decode step: token_out is not the argmax of logits")
+    eng.close()

@@ -203,14 +203,15 @@ def _resolve_layout(blk, layouts, kind):
     )
 
 
-def _swap_linears(submodule, linear_names, M, device, seed, cnt, init):
+def _swap_linears(submodule, linear_names, M, device, seed, cnt, init, keep_dense):
     for name in linear_names:
         old = getattr(submodule, name)
         if isinstance(old, NmSparseLinear):
             N, K = old.h, old.in_features
         else:
             N, K = old.weight.shape
-        dense_weight = None if (DECODE_ONLY or isinstance(old, NmSparseLinear)) else old.weight
+        keep = (not DECODE_ONLY) if keep_dense is None else keep_dense
+        dense_weight = old.weight if (keep and not isinstance(old, NmSparseLinear)) else None
         del old
         if torch.cuda.is_available():
             torch.cuda.empty_cache()
@@ -219,7 +220,8 @@ def _swap_linears(submodule, linear_names, M, device, seed, cnt, init):
     return cnt
 
 
-def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str = "reference"):
+def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str = "reference",
+                     keep_dense: bool | None = None):
     """Replace every decoder block's attention and MLP linears with
     NmSparseLinear (reference: src/spmv/nmsparse_linear.py:124-144).
 
@@ -228,6 +230,8 @@ def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str 
     device per block.  Returns the number of linears swapped.
     ``init="device"`` draws the weights on the GPU instead (same
     distribution, different numbers, much faster for multi-GB models).
+    ``keep_dense`` overrides NM_DECODE_ONLY for keeping the dense weight (used
+    by prefill with more than one token, :55-68).
     """
     cnt = 0
     for i, blk in enumerate(model.layers):
@@ -236,7 +240,7 @@ def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str 
             d = block_devices[i]
             blk_device = d if isinstance(d, str) else f"cuda:{d}"
         attn, attn_names = _resolve_layout(blk, _ATTENTION_LAYOUTS, "attention")
-        cnt = _swap_linears(attn, attn_names, M, blk_device, seed, cnt, init)
+        cnt = _swap_linears(attn, attn_names, M, blk_device, seed, cnt, init, keep_dense)
         mlp, mlp_names = _resolve_layout(blk, _MLP_LAYOUTS, "feed-forward")
-        cnt = _swap_linears(mlp, mlp_names, M, blk_device, seed, cnt, init)
+        cnt = _swap_linears(mlp, mlp_names, M, blk_device, seed, cnt, init, keep_dense)
     return cnt
