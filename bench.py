@@ -1,0 +1,394 @@
+"""Benchmark: batch-1 decode ms/token under a CUDA graph (the reference's
+headline metric), with the sparse GEMV's achieved HBM bandwidth as the
+roofline of the dominant kernel.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--model llama-3.1-8b] [--nm 32:64] [--ctx 512]
+
+Protocol (reference: benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:145-189):
+synthetic random-init weights, KV cache ~ N(0, 0.02) for CTX positions,
+token 123 at position CTX, one decode step (embedding, all layers, output
+head, greedy token) captured in a CUDA graph and replayed.  W untimed
+replays, then K timed replays bracketed by a barrier and a device
+synchronize, timed with CUDA events on the replay stream; every replay
+streams all weights (> 8 GB), far more than the 126 MB L2, so no flush is
+needed.  N > 1 runs tensor-parallel decode (one process per GPU, NCCL
+all-reduce after the o- and down-projections); the time is the max over
+ranks.
+
+The JSON line also carries:
+  e2e          the same metric through the public generation API with a
+               pinned host->device token copy and a device->host read of the
+               next token every step (positions advance);
+  roofline     the sparse GEMV kernel timed live in a plan holding only the
+               step's GEMV launches: algorithmic bytes / duration vs the
+               measured HBM copy bandwidth (MEASURED_PEAKS.json);
+  cpu_baseline the reference's torch CPU path (dense masked fp16 F.linear)
+               on a bounded sample of the same workload, on this host;
+  dense        the same engine with dense weights, and dense cuBLAS decode
+               (torch modules with nn.Linear captured in a CUDA graph).
+``--impl reference`` prints the CPU reference arm's line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "decode ms/token bs=1 (CUDA graph)"
+UNIT = "ms/token"
+# Published reference number for this exact metric and configuration:
+# Llama 3.1 8B, 32:64, CTX=512, fixed-context CUDA-graph decode, A100-SXM4-80GB
+# (reference README.md:93).
+PUBLISHED = {("llama-3.1-8b", "32:64"): (6.8521, "A100-SXM4-80GB", "README.md:93"),
+             ("qwen3-32b", "16:32"): (33.7054, "A100-SXM4-80GB", "README.md:118")}
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=50)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model", default="llama-3.1-8b")
+    p.add_argument("--nm", default="32:64", help="N:M pattern, or 'dense'")
+    p.add_argument("--ctx", type=int, default=int(os.environ.get("CTX", 512)))
+    p.add_argument("--e2e-steps", type=int, default=256)
+    p.add_argument("--prefetch", type=int, default=0, help="per-warp L2 look-ahead bytes inside a GEMV")
+    p.add_argument("--next-prefetch", type=int, default=0,
+                   help="bytes of the following GEMV's weights prefetched into L2 by each launch")
+    p.add_argument("--no-dense", action="store_true", help="skip the dense controls")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--cpu-layers", type=int, default=2)
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def measured_peaks() -> dict:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / "gemv_traffic.json"
+    if not f.exists():
+        return None
+    d = json.loads(f.read_text())
+    return d.get(workload)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def time_graph(graph, stream, steps: int, warmup: int, world: int) -> float:
+    """Mean ms per replay over ``steps`` timed replays; max over ranks.
+    ``stream`` must be the current stream (the one replay() launches on)."""
+    assert stream == torch.cuda.current_stream(), "time on the stream the graph replays on"
+    for _ in range(warmup):
+        graph.replay()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_reference_arm(args, world: int, rank: int) -> None:
+    """The reference's own CPU implementation of the path (torch CPU F.linear
+    on dense masked fp16 weights), timed on this host's cores."""
+    if rank != 0:
+        return
+    from oracle.decode_oracle import cpu_decode_sample
+    from spmv_decode_b200.model import ModelArgs
+
+    cfg = ModelArgs.from_name(args.model)
+    nm = None if args.nm == "dense" else tuple(int(v) for v in args.nm.split(":"))
+    threads = os.cpu_count() or 1
+    # Each "step" is one sampled token; keep the run bounded.
+    steps = max(1, min(args.steps, 5))
+    r = cpu_decode_sample(cfg, nm, args.ctx, sample_layers=args.cpu_layers, steps=steps, threads=threads,
+                          seed=args.seed)
+    v = r["ms_per_token"]
+    line = {
+        "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": 1, "ms_per_step": round(v, 3), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16 (torch CPU F.linear)", "data": "synthetic random-init weights",
+        "impl": "reference",
+        "config": {"workload": f"{args.model}-arch {args.nm} decode, ctx {args.ctx}, batch 1",
+                   "model": args.model, "nm": args.nm, "ctx": args.ctx, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": r["threads"], "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world == 1 and args.gpus > 1:
+        raise SystemExit("for --gpus > 1 launch with torch.distributed.run (one process per GPU)")
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+
+    from spmv_decode_b200 import _lib
+    from spmv_decode_b200.engine import DecodeEngine
+    from spmv_decode_b200.generate import build_model
+    from spmv_decode_b200.model import ModelArgs
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    nm = None if args.nm == "dense" else tuple(int(v) for v in args.nm.split(":"))
+    cfg = ModelArgs.from_name(args.model)
+    max_seq = args.ctx + 1 + args.e2e_steps + 8
+    t_build = time.time()
+    tp = None
+    if world > 1:
+        from spmv_decode_b200.tp import build_tp_engine
+
+        eng, tp = build_tp_engine(cfg, nm, world, rank, dev, max_seq=max_seq, seed=args.seed,
+                                  prefetch_bytes=args.prefetch, next_prefetch_bytes=args.next_prefetch,
+                                  history_len=max_seq)
+    else:
+        model = build_model(cfg, nm=nm, device=dev, seed=args.seed, init="device")
+        eng = DecodeEngine(model, max_seq, prefetch_bytes=args.prefetch, next_prefetch_bytes=args.next_prefetch,
+                           history_len=max_seq)
+    build_s = time.time() - t_build
+
+    # ---- headline: fixed-context graph replay --------------------------------
+    eng.fill_synthetic_cache(args.ctx, seed=args.seed)
+    eng.token_in.fill_(123)
+    graph = eng.capture(advance=False)
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(local_rank)
+    ms = time_graph(graph, stream, args.steps, args.warmup, world)
+    clk = clocks.stop()
+    assert torch.isfinite(eng.logits.float()).all(), "non-finite logits after replay"
+    launches_per_step = eng.size() - 1  # the plan holds the head twice (fixed / advancing)
+    dev_err = _lib.device_error()
+
+    # ---- e2e: public generation API with host I/O every step ------------------
+    from spmv_decode_b200.generate import GraphDecoder
+
+    gd = GraphDecoder(eng)
+    e2e_steps = min(args.e2e_steps, max_seq - args.ctx - 2)
+    tok_host = torch.tensor([123], dtype=torch.int64).pin_memory()
+    out_host = torch.zeros(1, dtype=torch.int64).pin_memory()
+    eng.pos.fill_(args.ctx)
+    for _ in range(3):
+        eng.token_in.copy_(tok_host, non_blocking=True)
+        gd.replay()
+        out_host.copy_(eng.token_out, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    eng.pos.fill_(args.ctx)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        eng.token_in.copy_(tok_host, non_blocking=True)
+        gd.replay()
+        out_host.copy_(eng.token_out, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        tok_host[0] = out_host[0]
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # ---- roofline: the sparse GEMV kernel timed live --------------------------
+    plan, gemv_bytes = eng.gemv_plan()
+    n_gemv = sum(1 for r in eng.gemv_records if not r["argmax"])
+
+    s2 = torch.cuda.Stream(dev)
+    s2.wait_stream(stream)
+    with torch.cuda.stream(s2):
+        for _ in range(3):
+            _lib.check(_lib.lib().nms_plan_launch(plan, 0, n_gemv, s2.cuda_stream))
+    stream.wait_stream(s2)
+    torch.cuda.synchronize()
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=s2):
+        _lib.check(_lib.lib().nms_plan_launch(plan, 0, n_gemv, s2.cuda_stream))
+    gemv_ms = time_graph(g2, stream, max(10, args.steps // 4), 5, world)
+    _lib.lib().nms_plan_destroy(plan)
+    peaks = measured_peaks()
+    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    workload = f"{args.model}-arch {args.nm} decode, ctx {args.ctx}, batch 1"
+    roofline = {"bound": "hbm", "kernel": "gemv_packed_kernel", "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "peak_source": peaks["source"], "traffic": profiled_traffic(workload),
+                "algorithmic_bytes_per_step": gemv_bytes, "launches_per_step": n_gemv,
+                "mean_launch_us": round(gemv_ms * 1e3 / n_gemv, 3)}
+    weight_bytes = sum(r["bytes"] for r in eng.gemv_records)  # incl. head
+    step_roofline = {"bytes_per_token": weight_bytes, "ideal_ms": round(weight_bytes / peaks["hbm_gbs"] / 1e6, 4),
+                     "frac": round(weight_bytes / peaks["hbm_gbs"] / 1e6 / ms, 4)}
+    del g2, graph, gd
+    eng.close()
+    del eng
+    if world == 1:
+        del model
+    torch.cuda.empty_cache()
+
+    # ---- dense controls ------------------------------------------------------
+    dense = None
+    if not args.no_dense and nm is not None and world == 1:
+        dense = {}
+        dmodel = build_model(cfg, nm=None, device=dev, seed=args.seed + 1, init="device")
+        deng = DecodeEngine(dmodel, args.ctx + 8, prefetch_bytes=args.prefetch,
+                            next_prefetch_bytes=args.next_prefetch)
+        deng.fill_synthetic_cache(args.ctx, seed=args.seed)
+        deng.token_in.fill_(123)
+        dg = deng.capture(advance=False)
+        dense["engine_dense_ms"] = round(time_graph(dg, stream, max(20, args.steps // 4), 10, world), 4)
+        del dg
+        deng.close()
+        del deng
+        torch.cuda.empty_cache()
+        # cuBLAS: the torch module path (nn.Linear -> cuBLAS, SDPA attention)
+        # captured in a CUDA graph, like the reference's dense baseline.
+        dmodel.setup_caches(1, args.ctx + 8)
+        for blk in dmodel.layers:
+            blk.attn.kv_cache.k_cache.normal_(std=0.02)
+            blk.attn.kv_cache.v_cache.normal_(std=0.02)
+        idx = torch.tensor([[123]], device=dev)
+        ipos = torch.tensor([args.ctx], device=dev)
+        with torch.inference_mode():
+            s3 = torch.cuda.Stream(dev)
+            s3.wait_stream(stream)
+            with torch.cuda.stream(s3):
+                for _ in range(3):
+                    torch.argmax(dmodel(None, idx, ipos)[0, -1])
+            stream.wait_stream(s3)
+            torch.cuda.synchronize()
+            g3 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g3, stream=s3):
+                torch.argmax(dmodel(None, idx, ipos)[0, -1])
+            dense["cublas_graph_ms"] = round(time_graph(g3, stream, max(20, args.steps // 4), 10, world), 4)
+        del g3, dmodel
+        torch.cuda.empty_cache()
+        dense["speedup_vs_engine_dense"] = round(dense["engine_dense_ms"] / ms, 3)
+        dense["speedup_vs_cublas"] = round(dense["cublas_graph_ms"] / ms, 3)
+
+    # ---- CPU baseline (rank 0, N=1) -----------------------------------------
+    cpu = None
+    if not args.no_cpu and world == 1 and rank == 0:
+        from oracle.decode_oracle import cpu_decode_sample
+
+        r = cpu_decode_sample(cfg, nm, args.ctx, sample_layers=args.cpu_layers, steps=3,
+                              threads=os.cpu_count(), seed=args.seed)
+        cpu = {"value": round(r["ms_per_token"], 3), "unit": UNIT, "cores": r["threads"], "kind": "port",
+               "sample": r["sample"]}
+
+    if rank == 0:
+        pub = PUBLISHED.get((args.model, args.nm))
+        line = {
+            "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None if pub is None else round(ms / pub[0], 4),
+            "dtype": "f16 (fp32 accumulate)",
+            "data": "synthetic: random-init weights N(0,0.02), KV cache N(0,0.02) (reference fixed-context protocol)",
+            "config": {"workload": workload, "model": args.model, "nm": args.nm, "ctx": args.ctx,
+                       "parallelism": f"tp{world}", "prefetch": args.prefetch, "next_prefetch": args.next_prefetch,
+                       "l2": "no flush: every replay streams all weights (>> 126 MB L2)"},
+            "e2e": {"value": round(e2e_ms, 4), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+                    "steps": e2e_steps, "note": "public generation API, host token in/out every step"},
+            "roofline": roofline,
+            "step_roofline": step_roofline,
+            "cpu_baseline": cpu,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "dense": dense,
+            "baseline_published": None if pub is None else {"value": pub[0], "hardware": pub[1], "source": pub[2]},
+            "build_s": round(build_s, 1),
+            "device_error": dev_err,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        del tp
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -136,7 +136,7 @@ typedef struct nms_gemv_fused_args {
   int64_t* token_out;
   int32_t amax_capacity;
   int32_t grid;           /* CTAs (0 = two per SM) */
-  int32_t prefetch_bytes; /* per-CTA L2 prefetch before the dependency wait */
+  int32_t prefetch_bytes; /* per-warp L2 look-ahead beyond the register ring (0 = off) */
   /* argmax generation hooks (each may be NULL): also write the token to
    * next_token; if pos is set, write token_history[*pos] = token (when
    * *pos < history_len) and then increment *pos.  Lets a captured decode
@@ -145,6 +145,13 @@ typedef struct nms_gemv_fused_args {
   int64_t* token_history;
   int64_t* pos;
   int64_t history_len;
+  /* Cross-launch L2 prefetch (optional): the weights of the launch that
+   * follows this one, as up to two byte ranges; every CTA prefetches the
+   * first next_prefetch_head bytes of its equal share of each range before
+   * its dependency wait, so the next launch starts on L2 hits. */
+  const void* next_prefetch[2];
+  int64_t next_prefetch_bytes[2];
+  int64_t next_prefetch_head;
 } nms_gemv_fused_args;
 
 int nms_gemv_fused_f16(const nms_gemv_fused_args* args, void* stream);
@@ -174,6 +181,9 @@ typedef struct nms_attention_args {
   float norm_eps;
   float scale; /* usually 1/sqrt(D) */
   int32_t flags; /* NMS_FLAG_PDL */
+  const void* next_prefetch[2]; /* as in nms_gemv_fused_args */
+  int64_t next_prefetch_bytes[2];
+  int64_t next_prefetch_head;
 } nms_attention_args;
 
 int nms_attention_decode_f16(const nms_attention_args* args, void* stream);

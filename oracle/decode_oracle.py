@@ -269,3 +269,76 @@ class OracleModel:
                 tokens.append(nxt)
                 cur = nxt
         return tokens, torch.stack(logits_all)
+
+
+def _masked_random(rows: int, K: int, m: Optional[int], std: float, gen: torch.Generator) -> torch.Tensor:
+    """Dense fp16 [rows, K] ~ N(0, std) with a shared 50% in-group mask
+    (all rows keep the same m/2 columns of every group of m), or unmasked
+    when m is None."""
+    W = (torch.randn(rows, K, generator=gen) * std).to(torch.float16)
+    if m is not None:
+        keys = torch.rand(K // m, m, generator=gen)
+        drop = keys.argsort(dim=1)[:, m // 2:]
+        cols = (torch.arange(K // m)[:, None] * m + drop).reshape(-1)
+        W[:, cols] = 0
+    return W
+
+
+def cpu_decode_sample(config, nm: Optional[tuple], ctx: int, sample_layers: int = 2, steps: int = 3,
+                      threads: Optional[int] = None, seed: int = 0) -> dict:
+    """Time the reference's torch CPU decode path on a bounded sample of a
+    workload: ``sample_layers`` decoder layers of the configuration's shapes
+    plus the full output head, dense masked fp16 weights multiplied with
+    F.linear (the reference's CPU path, microbench_triton_torchmv.py:210-211),
+    KV cache ~ N(0, 0.02) of length ``ctx``.  The per-token time of the whole
+    model is extrapolated as n_layer * (layer time) + head time."""
+    import time
+
+    if threads:
+        torch.set_num_threads(threads)
+    c = config
+    D = c.head_dim
+    m = None if nm is None else nm[1]
+    gen = torch.Generator().manual_seed(seed)
+    layers = []
+    for _ in range(sample_layers):
+        qkv_rows = (c.n_head + 2 * c.n_local_heads) * D
+        ones = torch.ones(c.dim, dtype=torch.float16)
+        qn = torch.ones(D, dtype=torch.float16) if c.qk_norm else None
+        layers.append(OracleLayer([_masked_random(qkv_rows, c.dim, m, 0.02, gen)],
+                                  _masked_random(c.dim, c.n_head * D, m, 0.02, gen),
+                                  _masked_random(c.intermediate_size, c.dim, m, 0.02, gen),
+                                  _masked_random(c.intermediate_size, c.dim, m, 0.02, gen),
+                                  _masked_random(c.dim, c.intermediate_size, m, 0.02, gen), ones, ones, qn, qn))
+    emb = (torch.randn(c.vocab_size, c.dim, generator=gen) * 0.02).to(torch.float16)
+    head = emb if c.tie_embeddings else (torch.randn(c.vocab_size, c.dim, generator=gen) * 0.02).to(torch.float16)
+    om = OracleModel(layers=layers, emb=emb, head=head, final_norm=torch.ones(c.dim, dtype=torch.float16),
+                     n_head=c.n_head, n_kv=c.n_local_heads, head_dim=D, eps=c.norm_eps,
+                     rope=rope_table(ctx + steps + 2, D, c.rope_base, c.rope_scaling, c.rope_style),
+                     style=c.rope_style, max_seq=ctx + steps + 2, linear_dtype=torch.float16)
+    for kc, vc in zip(om.k, om.v):
+        kc.normal_(0, 0.02, generator=gen)
+        vc.normal_(0, 0.02, generator=gen)
+    x = torch.randn(c.dim, generator=gen).to(torch.float16)
+    om.step(123, ctx)  # warm-up
+    t_step, t_head = [], []
+    for i in range(steps):
+        t0 = time.perf_counter()
+        om.step(123, ctx)
+        t1 = time.perf_counter()
+        om._linear(om.head, x)
+        t2 = time.perf_counter()
+        t_step.append(t1 - t0)
+        t_head.append(t2 - t1)
+    step_s = sorted(t_step)[len(t_step) // 2]
+    head_s = sorted(t_head)[len(t_head) // 2]
+    layer_s = max(step_s - head_s, 0.0) / sample_layers
+    return {
+        "ms_per_token": 1e3 * (c.n_layer * layer_s + head_s),
+        "layer_ms": 1e3 * layer_s,
+        "head_ms": 1e3 * head_s,
+        "threads": torch.get_num_threads(),
+        "sample": f"{sample_layers} of {c.n_layer} decoder layers + full output head, ctx {ctx}, "
+                  f"median of {steps} steps, dense masked fp16 F.linear; per-token time = "
+                  f"{c.n_layer} x layer + head",
+    }

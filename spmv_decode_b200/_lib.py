@@ -95,6 +95,9 @@ class NmsGemvFusedArgs(ctypes.Structure):
         ("token_history", c_void_p),
         ("pos", c_void_p),
         ("history_len", c_i64),
+        ("next_prefetch", c_void_p * 2),
+        ("next_prefetch_bytes", c_i64 * 2),
+        ("next_prefetch_head", c_i64),
     ]
 
 
@@ -117,6 +120,9 @@ class NmsAttentionArgs(ctypes.Structure):
         ("norm_eps", ctypes.c_float),
         ("scale", ctypes.c_float),
         ("flags", c_i32),
+        ("next_prefetch", c_void_p * 2),
+        ("next_prefetch_bytes", c_i64 * 2),
+        ("next_prefetch_head", c_i64),
     ]
 
 

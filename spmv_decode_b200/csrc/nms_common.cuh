@@ -76,6 +76,27 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) 
                : "memory");
 }
 
+// Cross-launch L2 prefetch: each of the two byte ranges (the next launch's
+// weights) is split into `nb` equal shares, and CTA `b` prefetches the first
+// `head` bytes of its share of each range -- the bytes the next launch's CTA
+// `b` reads first when both grids partition the rows the same way.  Pieces
+// are 16-byte aligned (ranges are whole packed rows) and at most 64 KB.
+__device__ __forceinline__ void prefetch_shares_l2(const char* const (&ptr)[2], const uint32_t (&bytes)[2],
+                                                   uint32_t head, unsigned b, unsigned nb) {
+  if (head == 0) return;
+  for (int r = 0; r < 2; ++r) {
+    if (ptr[r] == nullptr || bytes[r] == 0) continue;
+    const uint64_t len = bytes[r];
+    const uint64_t lo = (len * b / nb) & ~15ull;
+    const uint64_t hi = (b + 1 == nb) ? len : ((len * (b + 1) / nb) & ~15ull);
+    const uint64_t e = hi < lo + head ? hi : lo + head;
+    for (uint64_t q = lo; q + 16 <= e; q += 65536) {
+      const uint64_t n = (e - q) < 65536 ? (e - q) : 65536;
+      bulk_prefetch_l2(ptr[r] + q, (uint32_t)(n & ~15ull));
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Mixed-precision FMA: d = a*b + c with a, b fp16 and c, d fp32, one rounding
 // (the fp16*fp16 product is exact in fp32, so this equals fmaf(float(a),

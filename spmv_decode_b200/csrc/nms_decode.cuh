@@ -22,7 +22,7 @@ namespace nms {
 constexpr int kAttnThreads = 256;
 constexpr int kAttnD = 128;       // head_dim supported by this kernel
 constexpr int kAttnMaxGroup = 8;  // q heads per KV head (one warp each)
-constexpr int kAttnTile = 32;     // positions per tile
+constexpr int kAttnTile = 64;     // positions per tile (two per lane in the softmax)
 
 enum RopeStyle : int32_t { kRopeInterleaved = 0, kRopeHalf = 1 };
 
@@ -40,6 +40,9 @@ struct AttnParams {
   int32_t Hq, Hkv, S_max;
   int32_t rope_style;
   int32_t splits;       // CTAs per KV head (cluster size)
+  const char* next_pf[2];  // weights of the next launch (see prefetch_shares_l2)
+  uint32_t next_pf_bytes[2];
+  uint32_t next_pf_head;
 };
 
 // RMSNorm over one head held as 4 values per lane of a warp (fp32 math,
@@ -91,19 +94,26 @@ __device__ __forceinline__ void head_rope(float (&v)[4], const __half* rope_row,
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __grid_constant__ AttnParams p) {
-  constexpr int D = kAttnD, PT = kAttnTile, KS = D + 8;
-  __shared__ float sq[kAttnMaxGroup][D];
-  __shared__ __align__(16) __half sk[PT][KS];
-  __shared__ __align__(16) __half sv[PT][D];
+  constexpr int D = kAttnD, PT = kAttnTile, KS = D + 8, GM = kAttnMaxGroup;
+  constexpr int NT = kAttnThreads;
+  __shared__ float sq[GM][D];                 // q heads (values exactly fp16), pre-scaled
+  __shared__ __align__(16) __half sk[PT][KS];  // K tile (padded rows: conflict-free row reads)
+  __shared__ __align__(16) __half sv[PT][D];   // V tile
+  __shared__ float sp[GM][PT];                 // scores, then probabilities
   __shared__ __align__(16) __half knew[D];
   __shared__ __align__(16) __half vnew[D];
-  __shared__ float sm[kAttnMaxGroup], sl[kAttnMaxGroup];
-  __shared__ float so[kAttnMaxGroup][D];
+  __shared__ float sm[GM], sl[GM], scorr[GM];  // running max / sum / rescale per head
+  __shared__ float so[GM][D];                  // running (unnormalised) output
+  __shared__ float cm[16][GM], cl[16][GM];     // cluster combine: every rank's (m, l)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int G = p.Hq / p.Hkv;
 
+  if (tid == 0) {
+    const unsigned b = blockIdx.y * gridDim.x + blockIdx.x;
+    prefetch_shares_l2(p.next_pf, p.next_pf_bytes, p.next_pf_head, b, gridDim.x * gridDim.y);
+  }
   grid_dep_wait();
   const int64_t pos64 = *p.pos;
   if (pos64 < 0 || pos64 >= p.S_max) {  // uniform across the grid: every CTA reads the same value
@@ -117,18 +127,20 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __
   const bool has_new = (split == p.splits - 1);
   const __half* rope_row = p.rope + (size_t)pos * D;
 
-  // q heads of this KV group: norm + RoPE, kept as fp32 copies of fp16 values.
+  // q heads of this KV group: norm + RoPE; the softmax scale is folded in.
   if (warp < G) {
     const __half* qsrc = p.qkv + (size_t)(kvh * G + warp) * D;
     float v[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = h2f(qsrc[lane * 4 + e]);
+    const uint2 qv = *reinterpret_cast<const uint2*>(qsrc + lane * 4);
+    const float2 q0 = __half22float2(*reinterpret_cast<const __half2*>(&qv.x));
+    const float2 q1 = __half22float2(*reinterpret_cast<const __half2*>(&qv.y));
+    v[0] = q0.x; v[1] = q0.y; v[2] = q1.x; v[3] = q1.y;
     if (p.q_norm) head_rmsnorm(v, p.q_norm, lane, p.norm_eps);
     head_rope(v, rope_row, lane, p.rope_style);
 #pragma unroll
     for (int e = 0; e < 4; ++e) sq[warp][lane * 4 + e] = v[e];
   }
-  if (has_new && warp == kAttnMaxGroup - 2) {  // new k
+  if (has_new && warp == GM - 2) {  // new k: norm + RoPE, append to the cache
     const __half* ksrc = p.qkv + (size_t)p.Hq * D + (size_t)kvh * D;
     float v[4];
 #pragma unroll
@@ -142,7 +154,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __
       kdst[lane * 4 + e] = f2h(v[e]);
     }
   }
-  if (has_new && warp == kAttnMaxGroup - 1) {  // new v
+  if (has_new && warp == GM - 1) {  // new v: append to the cache
     const __half* vsrc = p.qkv + (size_t)(p.Hq + p.Hkv) * D + (size_t)kvh * D;
     __half* vdst = p.v_cache + ((size_t)kvh * p.S_max + pos) * D;
 #pragma unroll
@@ -151,18 +163,23 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __
       vdst[lane * 4 + e] = vsrc[lane * 4 + e];
     }
   }
+  for (int i = tid; i < GM * D; i += NT) (&so[0][0])[i] = 0.f;
+  if (tid < GM) {
+    sm[tid] = -INFINITY;
+    sl[tid] = 0.f;
+  }
   __syncthreads();
   grid_dep_launch_dependents();
 
-  float m_run = -INFINITY, l_run = 0.f;
-  float o[4] = {0.f, 0.f, 0.f, 0.f};
   const __half* kbase = p.k_cache + (size_t)kvh * p.S_max * D;
   const __half* vbase = p.v_cache + (size_t)kvh * p.S_max * D;
-
   for (int t0 = pb; t0 < pe; t0 += PT) {
     const int nt = min(PT, pe - t0);
-    // Load the K and V tiles (16-byte pieces; the new token comes from smem).
-    for (int c = tid; c < 2 * PT * (D / 8); c += kAttnThreads) {
+    // (a) K and V tiles in one batch of independent 16-byte loads.
+    constexpr int PIECES = 2 * PT * (D / 8);
+#pragma unroll
+    for (int it = 0; it < PIECES / NT; ++it) {
+      const int c = tid + it * NT;
       const int which = c / (PT * (D / 8));
       const int rem = c - which * PT * (D / 8);
       const int r = rem / (D / 8), q8 = rem % (D / 8);
@@ -172,8 +189,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __
         if (tpos == pos) {
           val = *reinterpret_cast<const uint4*>((which ? vnew : knew) + q8 * 8);
         } else {
-          const __half* src = (which ? vbase : kbase) + (size_t)tpos * D + q8 * 8;
-          val = __ldg(reinterpret_cast<const uint4*>(src));
+          val = __ldg(reinterpret_cast<const uint4*>((which ? vbase : kbase) + (size_t)tpos * D + q8 * 8));
         }
       }
       if (which == 0)
@@ -182,15 +198,17 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __
         *reinterpret_cast<uint4*>(&sv[r][q8 * 8]) = val;
     }
     __syncthreads();
-    if (warp < G) {
+    // (b) scores: one (head, position) pair per thread.
+    for (int i = tid; i < G * PT; i += NT) {
+      const int g = i / PT, r = i % PT;
       float s = -INFINITY;
-      if (lane < nt) {
+      if (r < nt) {
         float d0 = 0.f, d1 = 0.f;
-#pragma unroll 4
+#pragma unroll
         for (int q8 = 0; q8 < D / 8; ++q8) {
-          const uint4 kk = *reinterpret_cast<const uint4*>(&sk[lane][q8 * 8]);
-          const float4 qa = *reinterpret_cast<const float4*>(&sq[warp][q8 * 8]);
-          const float4 qb = *reinterpret_cast<const float4*>(&sq[warp][q8 * 8 + 4]);
+          const uint4 kk = *reinterpret_cast<const uint4*>(&sk[r][q8 * 8]);
+          const float4 qa = *reinterpret_cast<const float4*>(&sq[g][q8 * 8]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sq[g][q8 * 8 + 4]);
           const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
           const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
           const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&kk.z));
@@ -206,64 +224,71 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __
         }
         s = (d0 + d1) * p.scale;
       }
-      float mt = s;
+      sp[g][r] = s;
+    }
+    __syncthreads();
+    // (c) online softmax statistics: one warp per head.
+    if (warp < G) {
+      static_assert(PT == 64, "two positions per lane");
+      const float s0 = sp[warp][lane], s1 = sp[warp][lane + 32];
+      float mt = fmaxf(s0, s1);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-      const float m_new = fmaxf(m_run, mt);
-      const float corr = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
-      const float pe_ = (lane < nt) ? expf(s - m_new) : 0.f;
-      l_run = l_run * corr + warp_reduce_sum(pe_);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[e] *= corr;
-      for (int j = 0; j < nt; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, pe_, j);
-        const uint2 vv = *reinterpret_cast<const uint2*>(&sv[j][lane * 4]);
-        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vv.x));
-        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vv.y));
-        o[0] = fmaf(pj, v0.x, o[0]);
-        o[1] = fmaf(pj, v0.y, o[1]);
-        o[2] = fmaf(pj, v1.x, o[2]);
-        o[3] = fmaf(pj, v1.y, o[3]);
+      const float m_old = sm[warp];
+      const float m_new = fmaxf(m_old, mt);
+      const float p0 = (lane < nt) ? expf(s0 - m_new) : 0.f;
+      const float p1 = (lane + 32 < nt) ? expf(s1 - m_new) : 0.f;
+      const float tot = warp_reduce_sum(p0 + p1);
+      sp[warp][lane] = p0;
+      sp[warp][lane + 32] = p1;
+      if (lane == 0) {
+        const float corr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+        scorr[warp] = corr;
+        sl[warp] = sl[warp] * corr + tot;
+        sm[warp] = m_new;
       }
-      m_run = m_new;
+    }
+    __syncthreads();
+    // (d) P*V: (head, dim) pairs spread over the CTA.
+    for (int i = tid; i < G * D; i += NT) {
+      const int g = i / D, d = i - g * D;
+      float acc = so[g][d] * scorr[g];
+      for (int r = 0; r < nt; ++r) acc = fmaf(sp[g][r], h2f(sv[r][d]), acc);
+      so[g][d] = acc;
     }
     __syncthreads();
   }
 
-  if (warp < G) {
-    if (lane == 0) {
-      sm[warp] = m_run;
-      sl[warp] = l_run;
-    }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) so[warp][lane * 4 + e] = o[e];
-  }
-
+  // Cluster combine, distributed: rank r finalises dims [r*D/splits, ...).
   if (p.splits > 1) {
     cluster_sync_all();
-    if (split == 0) {
-      for (int c = tid; c < G * D; c += kAttnThreads) {
-        const int g = c / D, d = c - g * D;
-        float M = -INFINITY;
-        for (int r = 0; r < p.splits; ++r) M = fmaxf(M, r == 0 ? sm[g] : ld_dsmem_f32(&sm[g], (uint32_t)r));
-        float Lsum = 0.f, O = 0.f;
-        for (int r = 0; r < p.splits; ++r) {
-          const float mr = r == 0 ? sm[g] : ld_dsmem_f32(&sm[g], (uint32_t)r);
-          if (mr == -INFINITY) continue;
-          const float lr = r == 0 ? sl[g] : ld_dsmem_f32(&sl[g], (uint32_t)r);
-          const float orr = r == 0 ? so[g][d] : ld_dsmem_f32(&so[g][d], (uint32_t)r);
-          const float f = expf(mr - M);
-          Lsum = fmaf(lr, f, Lsum);
-          O = fmaf(orr, f, O);
-        }
-        p.y[(size_t)(kvh * G + g) * D + d] = f2h(O / Lsum);
-      }
+    for (int i = tid; i < p.splits * G; i += NT) {
+      const int r = i / G, g = i - r * G;
+      cm[r][g] = (r == split) ? sm[g] : ld_dsmem_f32(&sm[g], (uint32_t)r);
+      cl[r][g] = (r == split) ? sl[g] : ld_dsmem_f32(&sl[g], (uint32_t)r);
     }
-    cluster_sync_all();
-  } else {
     __syncthreads();
-    for (int c = tid; c < G * D; c += kAttnThreads) {
-      const int g = c / D, d = c - g * D;
+    const int dpr = (D + p.splits - 1) / p.splits;
+    const int d0 = split * dpr, d1 = min(D, d0 + dpr);
+    const int nd = max(0, d1 - d0);
+    for (int i = tid; i < G * nd; i += NT) {
+      const int g = i / nd, d = d0 + (i - g * nd);
+      float M = -INFINITY;
+      for (int r = 0; r < p.splits; ++r) M = fmaxf(M, cm[r][g]);
+      float Lsum = 0.f, O = 0.f;
+      for (int r = 0; r < p.splits; ++r) {
+        if (cm[r][g] == -INFINITY) continue;
+        const float f = expf(cm[r][g] - M);
+        const float orr = (r == split) ? so[g][d] : ld_dsmem_f32(&so[g][d], (uint32_t)r);
+        Lsum = fmaf(cl[r][g], f, Lsum);
+        O = fmaf(orr, f, O);
+      }
+      p.y[(size_t)(kvh * G + g) * D + d] = f2h(O / Lsum);
+    }
+    cluster_sync_all();  // keep every rank's shared memory alive until all reads are done
+  } else {
+    for (int i = tid; i < G * D; i += NT) {
+      const int g = i / D, d = i - g * D;
       p.y[(size_t)(kvh * G + g) * D + d] = f2h(so[g][d] / sl[g]);
     }
   }

@@ -60,7 +60,10 @@ struct GemvParams {
   int32_t w_pad;  // packed row stride, multiple of 16*L
   int32_t rows_total;  // concat: sum of segment rows; paired: rows of each segment
   int32_t row_groups;  // ceil(rows_total / RG)
-  int32_t prefetch_bytes;  // per-CTA bulk L2 prefetch issued before grid_dep_wait
+  int32_t pf_items;        // per-warp L2 look-ahead (work items of 1 KB) ahead of the register ring
+  const char* next_pf[2];  // weights of the next launch (see prefetch_shares_l2)
+  uint32_t next_pf_bytes[2];
+  uint32_t next_pf_head;
   const __half* x;
   const __half* x2;
   const __half* norm_w;
@@ -327,6 +330,31 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_packed_kernel(const __gr
     }
   }
 
+  // L2 look-ahead beyond the register ring (lane 0 issues bulk prefetches of
+  // whole chunk runs; every lane tracks the cursor so control stays uniform).
+  auto pf_range = [&](int ta, int tb) {
+    if (lane != 0) return;
+    int vg = ta / cpr, c = ta - vg * cpr;
+    while (ta < tb) {
+      const int cend = min(cpr, c + (tb - ta));
+#pragma unroll
+      for (int sg = 0; sg < RG; ++sg) {
+        const LaneRow r = lane_row(p, paired, g0, ng, vg, RG, sg);
+        if (r.valid)
+          bulk_prefetch_l2(p.seg[r.segi].w + (size_t)r.lrow * p.w_pad + (size_t)c * CH, (uint32_t)(cend - c) * CH * 2);
+      }
+      ta += cend - c;
+      c = 0;
+      ++vg;
+    }
+  };
+  int pf_next = min(t1, t0 + U);
+  if (p.pf_items > 0) {
+    const int e = min(t1, pf_next + p.pf_items);
+    pf_range(pf_next, e);
+    pf_next = e;
+  }
+
   const bool idx_bulk = !dense && ((p.w & 15) == 0);
   const bool x_bulk = (p.prologue == kProPlain) && ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0) &&
                       ((p.K & 7) == 0);
@@ -343,16 +371,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_packed_kernel(const __gr
         mbar_arrive_expect_tx(&s.bar[0], 0);
       }
     }
-    if (p.prefetch_bytes > 0 && t1 > t0) {
-      // Deeper look-ahead than the register ring: this CTA's next weights into L2.
-      const int pre_vg = min(vgroups - 1, l_vg);
-      const LaneRow r = lane_row(p, paired, g0, ng, pre_vg, RG, 0);
-      const __half* a = p.seg[r.segi].w + (size_t)r.lrow * p.w_pad;
-      const size_t seg_end_rows = paired ? (size_t)p.rows_total : (size_t)p.seg[r.segi].rows;
-      const size_t avail = (seg_end_rows - (size_t)r.lrow) * (size_t)p.w_pad * 2;
-      uint32_t bytes = (uint32_t)min((size_t)p.prefetch_bytes, avail) & ~15u;
-      if (bytes) bulk_prefetch_l2(a, bytes);
-    }
+    // This CTA's share of the next launch's first weights, into L2.
+    prefetch_shares_l2(p.next_pf, p.next_pf_bytes, p.next_pf_head, blockIdx.x, gridDim.x);
   }
   for (int v = tid; v < vgroups * RG; v += kGemvThreads) s.acc[v] = 0.f;
   __syncthreads();  // barrier init visible before anyone polls it
@@ -375,13 +395,37 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_packed_kernel(const __gr
     }
   } else {
     float ss = 0.f;
-    for (int i = tid; i < p.K; i += kGemvThreads) {
-      float v = h2f(p.x[i]);
-      if (p.prologue == kProResidNorm && p.x2 != nullptr) v = h2f(f2h(v + h2f(p.x2[i])));
-      const __half hv = f2h(v);
-      s.xs[i] = hv;
-      const float vr = h2f(hv);
-      ss = fmaf(vr, vr, ss);
+    const bool vec = ((p.K & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0) &&
+                     (p.x2 == nullptr || (reinterpret_cast<uintptr_t>(p.x2) & 15u) == 0);
+    if (vec) {
+      // 16-byte pieces: one load of x (and x2) per thread for K <= 4096.
+      for (int i8 = tid; i8 < p.K / 8; i8 += kGemvThreads) {
+        const uint4 a = *reinterpret_cast<const uint4*>(p.x + (size_t)i8 * 8);
+        uint4 b = make_uint4(0u, 0u, 0u, 0u);
+        const bool add = (p.prologue == kProResidNorm && p.x2 != nullptr);
+        if (add) b = *reinterpret_cast<const uint4*>(p.x2 + (size_t)i8 * 8);
+        const __half* ah = reinterpret_cast<const __half*>(&a);
+        const __half* bh = reinterpret_cast<const __half*>(&b);
+        uint4 o;
+        __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const __half hv = add ? f2h(h2f(ah[e]) + h2f(bh[e])) : ah[e];
+          oh[e] = hv;
+          const float vr = h2f(hv);
+          ss = fmaf(vr, vr, ss);
+        }
+        *reinterpret_cast<uint4*>(s.xs + (size_t)i8 * 8) = o;
+      }
+    } else {
+      for (int i = tid; i < p.K; i += kGemvThreads) {
+        float v = h2f(p.x[i]);
+        if (p.prologue == kProResidNorm && p.x2 != nullptr) v = h2f(f2h(v + h2f(p.x2[i])));
+        const __half hv = f2h(v);
+        s.xs[i] = hv;
+        const float vr = h2f(hv);
+        ss = fmaf(vr, vr, ss);
+      }
     }
     if (p.prologue == kProResidNorm) {
       const float tot = block_reduce_sum(ss, s.red);
@@ -471,6 +515,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_packed_kernel(const __gr
             l_valid = r.valid;
             l_ptr = p.seg[r.segi].w + (size_t)r.lrow * p.w_pad + li * 16;
           }
+        }
+        if (p.pf_items > 0 && pf_next < t1 && pf_next - t <= U + p.pf_items / 2) {
+          const int e = min(t1, pf_next + max(1, p.pf_items / 2));
+          pf_range(pf_next, e);
+          pf_next = e;
         }
         // Advance the consume cursor; flush at the end of a row-group or range.
         const bool row_end = (++c_c == cpr);

@@ -210,6 +210,22 @@ int check_nm(int64_t K, int64_t w, int32_t n, int32_t m) {
   return NMS_OK;
 }
 
+// Validate and copy a cross-launch prefetch description.
+int fill_next_prefetch(const void* const (&src)[2], const int64_t (&bytes)[2], int64_t head, const char* (&dst)[2],
+                       uint32_t (&dbytes)[2], uint32_t& dhead) {
+  for (int r = 0; r < 2; ++r) {
+    dst[r] = static_cast<const char*>(src[r]);
+    if (bytes[r] < 0 || bytes[r] > 0xFFFFFFF0ll) return fail(NMS_ERR_VALUE, "next_prefetch_bytes[%d] out of range", r);
+    if (src[r] == nullptr && bytes[r] != 0) return fail(NMS_ERR_VALUE, "next_prefetch[%d] is null", r);
+    if (src[r] != nullptr && (!aligned(src[r], 16) || (bytes[r] & 15) != 0))
+      return fail(NMS_ERR_VALUE, "next_prefetch[%d] must be 16-byte aligned with a multiple-of-16 size", r);
+    dbytes[r] = (uint32_t)bytes[r];
+  }
+  if (head < 0 || head > (1 << 30)) return fail(NMS_ERR_VALUE, "next_prefetch_head out of range");
+  dhead = (uint32_t)head;
+  return NMS_OK;
+}
+
 // Build the record of a packed-layout GEMV launch (all fused variants).
 int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
   if (a == nullptr) return fail(NMS_ERR_VALUE, "args is null");
@@ -289,7 +305,10 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
   p.w_pad = (int32_t)w_pad;
   p.rows_total = (int32_t)rows_total;
   p.row_groups = (int32_t)((rows_total + RG - 1) / RG);
-  p.prefetch_bytes = a->prefetch_bytes;
+  p.pf_items = a->prefetch_bytes / 1024;  // one work item streams 1 KB (32 lanes x 32 bytes)
+  rc = fill_next_prefetch(a->next_prefetch, a->next_prefetch_bytes, a->next_prefetch_head, p.next_pf,
+                          p.next_pf_bytes, p.next_pf_head);
+  if (rc) return rc;
   p.x = static_cast<const __half*>(a->x);
   p.x2 = static_cast<const __half*>(a->x2);
   p.norm_w = static_cast<const __half*>(a->norm_weight);
@@ -345,8 +364,8 @@ int prepare_attention(const nms_attention_args* a, LaunchRec* rec) {
   if (rc) return rc;
   int splits = a->splits;
   if (splits <= 0) {
-    splits = (2 * dev->num_sms + a->Hkv - 1) / a->Hkv;
-    if (splits > 8) splits = 8;
+    splits = (dev->num_sms + a->Hkv - 1) / a->Hkv;
+    if (splits > 16) splits = 16;
     if (splits < 1) splits = 1;
   }
   if (splits > 16) return fail(NMS_ERR_VALUE, "splits=%d > 16", splits);
@@ -366,6 +385,9 @@ int prepare_attention(const nms_attention_args* a, LaunchRec* rec) {
   p.S_max = a->S_max;
   p.rope_style = a->rope_style;
   p.splits = splits;
+  rc = fill_next_prefetch(a->next_prefetch, a->next_prefetch_bytes, a->next_prefetch_head, p.next_pf,
+                          p.next_pf_bytes, p.next_pf_head);
+  if (rc) return rc;
   rec->kind = LaunchRec::kAttention;
   rec->grid = dim3(splits, a->Hkv);
   rec->block = dim3(nms::kAttnThreads);

@@ -57,7 +57,7 @@ class DecodeEngine:
     """Batch-1 decode state + native plan for one model on one device."""
 
     def __init__(self, model: Transformer, max_seq_length: int, *, pdl: bool = True, prefetch_bytes: int = 0,
-                 attn_splits: int = 0, history_len: int = 0,
+                 next_prefetch_bytes: int = 0, attn_splits: int = 0, history_len: int = 0,
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None, tp_rank: int = 0, tp_size: int = 1,
                  local_heads: Optional[tuple] = None):
         c = model.config
@@ -68,7 +68,8 @@ class DecodeEngine:
             raise ValueError("DecodeEngine needs the model on a CUDA device")
         self.device = dev
         self.pdl = pdl
-        self.prefetch_bytes = int(prefetch_bytes)
+        self.prefetch_bytes = int(prefetch_bytes)  # per-warp L2 look-ahead inside a GEMV
+        self.next_prefetch_bytes = int(next_prefetch_bytes)  # L2 prefetch of the following GEMV's weights
         self.allreduce = allreduce
         self.tp_rank, self.tp_size = tp_rank, tp_size
         Hq, Hkv = local_heads if local_heads is not None else (c.n_head, c.n_local_heads)
@@ -113,6 +114,8 @@ class DecodeEngine:
             self._plan = ctypes.c_void_p()
             _lib.check(_lib.lib().nms_plan_create(ctypes.byref(self._plan)), "nms_plan_create")
             self.cut_points: List[int] = []  # plan indices after which an all-reduce runs
+            self.gemv_records: List[dict] = []
+            self._pending: List[tuple] = []  # launches in step order, added to the plan by _finalize
             self._build(model, attn_splits)
 
     # ------------------------------------------------------------------ build
@@ -163,7 +166,28 @@ class DecodeEngine:
                 a.pos = self.pos.data_ptr()
                 a.token_history = self.history.data_ptr()
                 a.history_len = self.history.numel()
-        _lib.check(_lib.lib().nms_plan_add_gemv(self._plan, ctypes.byref(a)), "nms_plan_add_gemv")
+        self._pending.append(("gemv", a, segs))
+        # Algorithmic bytes of this launch: kept values, mask offsets, the
+        # input vector(s) and the output (the roofline's traffic model).
+        bytes_ = sum(s["rows"] * s["w"] * 2 + (0 if s["dense"] else s["w"]) for s in segs)
+        bytes_ += s0["K"] * 2 * (2 if x2 is not None else 1) + (segs[0]["rows"] if swiglu else
+                                                               sum(s["rows"] for s in segs)) * 2
+        if not argmax or not advance:
+            self.gemv_records.append(dict(args=a, bytes=bytes_, dense=s0["dense"], argmax=argmax,
+                                          shape=(sum(s["rows"] for s in segs), s0["K"])))
+
+    def gemv_plan(self, include_head: bool = False):
+        """A separate plan holding only this step's GEMV launches (same
+        weights and arguments, in step order), for timing the GEMV kernel."""
+        plan = ctypes.c_void_p()
+        _lib.check(_lib.lib().nms_plan_create(ctypes.byref(plan)))
+        total = 0
+        for r in self.gemv_records:
+            if r["argmax"] and not include_head:
+                continue
+            _lib.check(_lib.lib().nms_plan_add_gemv(plan, ctypes.byref(r["args"])))
+            total += r["bytes"]
+        return plan, total
 
     def _build(self, model: Transformer, attn_splits: int):
         c = self.config
@@ -172,9 +196,8 @@ class DecodeEngine:
         if emb.dtype != torch.float16:
             raise TypeError("model must be float16 (the reference decode path is fp16)")
         self.emb = emb
-        _lib.check(L.nms_plan_add_embedding(self._plan, emb.data_ptr(), self.token_in.data_ptr(),
-                                            self.x_emb.data_ptr(), c.dim, emb.shape[0], self._flags()),
-                   "nms_plan_add_embedding")
+        self._pending.append(("emb", (emb.data_ptr(), self.token_in.data_ptr(), self.x_emb.data_ptr(), c.dim,
+                                      emb.shape[0], self._flags()), None))
         for li, blk in enumerate(model.layers):
             attn, ffn = blk.attn, blk.ffn
             qkv_lins = [attn.wqkv] if c.attn_layout == "fused" else [attn.q_proj, attn.k_proj, attn.v_proj]
@@ -197,24 +220,56 @@ class DecodeEngine:
             aa.norm_eps = float(attn.q_norm.eps) if qn is not None else 0.0
             aa.scale = 1.0 / math.sqrt(c.head_dim)
             aa.flags = self._flags()
-            _lib.check(L.nms_plan_add_attention(self._plan, ctypes.byref(aa)), "nms_plan_add_attention")
+            self._pending.append(("attn", aa, None))
             o_lin = attn.wo if c.attn_layout == "fused" else attn.o_proj
             self._add_gemv([o_lin], x=self.y_attn, out=self.y_o)
-            self.cut_points.append(self.size())
+            self.cut_points.append(len(self._pending))
             gate, up, down = ((ffn.w1, ffn.w3, ffn.w2) if c.attn_layout == "fused"
                               else (ffn.gate_proj, ffn.up_proj, ffn.down_proj))
             self._add_gemv([gate, up], x=self.x_buf, x2=self.y_o, norm=self._h(blk.norm2.weight), eps=blk.norm2.eps,
                            resid_out=self.h_buf, out=self.act, swiglu=True)
             self._add_gemv([down], x=self.act, out=self.y_down)
-            self.cut_points.append(self.size())
-        self._head_index = self.size()
+            self.cut_points.append(len(self._pending))
+        self._head_index = len(self._pending)
         self._final_norm = self._h(model.norm.weight)
         self._head_args = dict(x=self.h_buf, x2=self.y_down, norm=self._final_norm, eps=model.norm.eps,
                                out=self.logits, argmax=True)
         head = _HeadLinear(model.output_weight)
         self._add_gemv([head], advance=False, **self._head_args)
         self._add_gemv([head], advance=True, **self._head_args)  # variant used by generate()
-        self._plan_len = self._head_index + 1
+        self._finalize()
+
+    def _finalize(self) -> None:
+        """Give every launch the weight ranges of the GEMV that follows it
+        (the head's successor is the next step's first GEMV) for the
+        cross-launch L2 prefetch, then add the launches to the plan."""
+        L = _lib.lib()
+        sms = _lib.num_sms()
+        gemv_at = [i for i, e in enumerate(self._pending) if e[0] == "gemv"]
+        for i, (kind, a, segs) in enumerate(self._pending):
+            nxt = next((j for j in gemv_at if j > i and j != self._head_index + 1), None)
+            if nxt is None or (i >= self._head_index):
+                nxt = gemv_at[0]
+            if kind != "emb" and self.next_prefetch_bytes > 0:
+                nsegs = self._pending[nxt][2][:2]
+                if kind == "gemv":
+                    nb = 2 * sms
+                else:
+                    nb = a.Hkv * (a.splits if a.splits > 0 else min(16, -(-sms // a.Hkv)))
+                head = -(-self.next_prefetch_bytes // (nb * len(nsegs)))
+                head = (head + 15) // 16 * 16
+                for r, sg in enumerate(nsegs):
+                    a.next_prefetch[r] = sg["packed"].data_ptr()
+                    a.next_prefetch_bytes[r] = sg["rows"] * sg["w_pad"] * 2
+                a.next_prefetch_head = head
+            if kind == "gemv":
+                _lib.check(L.nms_plan_add_gemv(self._plan, ctypes.byref(a)), "nms_plan_add_gemv")
+            elif kind == "attn":
+                _lib.check(L.nms_plan_add_attention(self._plan, ctypes.byref(a)), "nms_plan_add_attention")
+            else:
+                _lib.check(L.nms_plan_add_embedding(self._plan, *a), "nms_plan_add_embedding")
+        self._keep_args = self._pending
+        self._pending = []
 
     def size(self) -> int:
         n = ctypes.c_int32()
