@@ -194,6 +194,27 @@ int nms_embedding_f16(const void* table, const int64_t* token, void* x, int64_t 
                       void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Output head + greedy token without any allocation (no counterpart in the
+ * reference, which allocates its scratch per call, triton_spmv.py:285).
+ * Same computation as nms_gemv_fused_f16 with NMS_FLAG_DENSE and
+ * NMS_EPI_ARGMAX: logits = head_weight [vocab, K] x rmsnorm(x + x2) (the
+ * norm prologue runs when norm_weight is not NULL; x2 may be NULL), and
+ * *token_out = argmax(logits), lowest index on ties.  For callers that cannot
+ * allocate device memory per call -- a serving runtime that has reserved the
+ * whole GPU for its own pools, or a bare C FFI caller without a caching
+ * allocator, where a cudaMalloc/cudaFree pair per token would synchronize the
+ * device and cost more than the head itself.  Its argmax scratch is a static
+ * 8.5 KB device array inside the library (partials of at most 1024 CTAs;
+ * larger launches return NMS_ERR_VALUE).  The first call on each device looks
+ * up that array's device address and should come before any stream capture.
+ * Calls share the array: calls that overlap on the GPU (other streams, other
+ * threads) race and must be serialized by the caller.
+ * ------------------------------------------------------------------------- */
+int nms_gemv_argmax_noalloc_f16(const void* x, const void* x2, const void* norm_weight, float eps,
+                                const void* head_weight, int64_t vocab, int64_t K, void* logits, int64_t* token_out,
+                                void* stream);
+
+/* ---------------------------------------------------------------------------
  * Launch plans: a native executor for one decode step.  Launches are
  * validated and frozen when added; nms_plan_launch replays a range of them
  * on a stream with no per-launch validation, so a decode step costs one

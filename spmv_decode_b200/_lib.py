@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "nms_gemv_fused_f16",
     "nms_attention_decode_f16",
     "nms_embedding_f16",
+    "nms_gemv_argmax_noalloc_f16",
     "nms_plan_create",
     "nms_plan_destroy",
     "nms_plan_add_gemv",
@@ -145,6 +146,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "nms_gemv_fused_f16": (I32, [ctypes.POINTER(NmsGemvFusedArgs), P]),
         "nms_attention_decode_f16": (I32, [ctypes.POINTER(NmsAttentionArgs), P]),
         "nms_embedding_f16": (I32, [P, P, P, I64, I64, I32, P]),
+        "nms_gemv_argmax_noalloc_f16": (I32, [P, P, P, ctypes.c_float, P, I64, I64, P, P, P]),
         "nms_plan_create": (I32, [ctypes.POINTER(P)]),
         "nms_plan_destroy": (I32, [P]),
         "nms_plan_add_gemv": (I32, [P, ctypes.POINTER(NmsGemvFusedArgs)]),

@@ -410,6 +410,40 @@ int prepare_embedding(const void* table, const int64_t* token, void* x, int64_t 
   return NMS_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Scratch of nms_gemv_argmax_noalloc_f16: the argmax partials of up to
+// kNoAllocMaxCtas CTAs and the completion counter, in a file-scope device
+// array instead of caller- or library-allocated memory.  Every GPU that loads
+// this library holds it (8.5 KB) until the process exits.
+constexpr int kNoAllocMaxCtas = 1024;
+constexpr size_t kNoAllocValOff = 0;
+constexpr size_t kNoAllocIdxOff = kNoAllocValOff + sizeof(float) * kNoAllocMaxCtas;
+constexpr size_t kNoAllocCounterOff = kNoAllocIdxOff + sizeof(int32_t) * kNoAllocMaxCtas;
+constexpr size_t kNoAllocBytes = 8448;
+static_assert(kNoAllocCounterOff + sizeof(uint32_t) <= kNoAllocBytes, "no-alloc scratch layout");
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (host code may not use the symbol itself as a pointer).
+unsigned char* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NMS_ERR_VALUE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return NMS_OK;
+}
+
 }  // namespace
 
 struct nms_plan {
@@ -574,6 +608,60 @@ int nms_embedding_f16(const void* table, const int64_t* token, void* x, int64_t 
   int rc = prepare_embedding(table, token, x, K, vocab, flags, &rec);
   if (rc) return rc;
   return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int nms_gemv_argmax_noalloc_f16(const void* x, const void* x2, const void* norm_weight, float eps,
+                                const void* head_weight, int64_t vocab, int64_t K, void* logits, int64_t* token_out,
+                                void* stream) {
+  if (!x || !head_weight || !logits || !token_out) return fail(NMS_ERR_VALUE, "null pointer argument");
+  if (vocab <= 0 || vocab > (1 << 30)) return fail(NMS_ERR_VALUE, "vocab=%lld out of range", (long long)vocab);
+  if (K <= 0 || K % 64 != 0) return fail(NMS_ERR_VALUE, "K=%lld must be a positive multiple of 64", (long long)K);
+  const DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  // One CTA per (up to) two SMs' worth of rows; the scratch holds
+  // kNoAllocMaxCtas partials, so larger launches are refused.
+  const int L = pick_lanes_per_row(K);
+  const int64_t row_groups = (vocab + (32 / L) - 1) / (32 / L);
+  const int64_t grid = row_groups < (int64_t)dev->num_sms * kGemvCtasPerSm ? row_groups
+                                                                          : (int64_t)dev->num_sms * kGemvCtasPerSm;
+  if (grid > kNoAllocMaxCtas)
+    return fail(NMS_ERR_VALUE, "launch needs %lld argmax partials; the static scratch holds %d", (long long)grid,
+                kNoAllocMaxCtas);
+  unsigned char* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  nms_gemv_fused_args a;
+  memset(&a, 0, sizeof(a));
+  a.seg[0].packed = head_weight;
+  a.seg[0].rows = vocab;
+  a.nseg = 1;
+  a.epilogue = NMS_EPI_ARGMAX;
+  a.prologue = norm_weight ? NMS_PRO_RESID_RMSNORM : NMS_PRO_PLAIN;
+  a.flags = NMS_FLAG_DENSE;
+  a.K = K;
+  a.w = K;
+  a.w_pad = K;
+  a.x = x;
+  a.x2 = norm_weight ? x2 : nullptr;
+  a.norm_weight = norm_weight;
+  a.eps = eps;
+  a.out = logits;
+  a.amax_val = reinterpret_cast<float*>(scratch + kNoAllocValOff);
+  a.amax_idx = reinterpret_cast<int32_t*>(scratch + kNoAllocIdxOff);
+  a.amax_counter = reinterpret_cast<uint32_t*>(scratch + kNoAllocCounterOff);
+  a.token_out = token_out;
+  a.amax_capacity = kNoAllocMaxCtas;
+  a.grid = (int32_t)grid;
+  LaunchRec rec;
+  rc = prepare_gemv(&a, &rec);
+  if (rc) return rc;
+  // The counter must start at zero; an earlier call leaves it at zero when it
+  // completes, and this clears it after an aborted one.
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(scratch + kNoAllocCounterOff, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(no-alloc counter)");
+  return launch_rec(rec, st);
 }
 
 int nms_plan_create(nms_plan** out) {
