@@ -72,6 +72,8 @@ def parse_args():
     p.add_argument("--no-dense", action="store_true", help="skip the dense controls")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--cpu-layers", type=int, default=2)
+    p.add_argument("--mode", choices=["auto", "persistent", "plan"], default="auto",
+                   help="decode-step executor: one persistent kernel or a per-kernel launch plan")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -228,7 +230,7 @@ def main():
     else:
         model = build_model(cfg, nm=nm, device=dev, seed=args.seed, init="device")
         eng = DecodeEngine(model, max_seq, prefetch_bytes=args.prefetch, next_prefetch_bytes=args.next_prefetch,
-                           history_len=max_seq)
+                           history_len=max_seq, mode=args.mode)
     build_s = time.time() - t_build
 
     # ---- headline: fixed-context graph replay --------------------------------
@@ -240,7 +242,10 @@ def main():
     ms = time_graph(graph, stream, args.steps, args.warmup, world)
     clk = clocks.stop()
     assert torch.isfinite(eng.logits.float()).all(), "non-finite logits after replay"
-    launches_per_step = eng.size() - 1  # the plan holds the head twice (fixed / advancing)
+    # Kernels of this library per step: one persistent kernel, or the plan's
+    # launches (the plan holds the head twice: fixed and advancing variants).
+    launches_per_step = 1 if eng.mode == "persistent" else eng.size() - 1
+    engine_mode = eng.mode
     dev_err = _lib.device_error()
 
     # ---- e2e: public generation API with host I/O every step ------------------
@@ -316,7 +321,7 @@ def main():
         dense = {}
         dmodel = build_model(cfg, nm=None, device=dev, seed=args.seed + 1, init="device")
         deng = DecodeEngine(dmodel, args.ctx + 8, prefetch_bytes=args.prefetch,
-                            next_prefetch_bytes=args.next_prefetch)
+                            next_prefetch_bytes=args.next_prefetch, mode=args.mode)
         deng.fill_synthetic_cache(args.ctx, seed=args.seed)
         deng.token_in.fill_(123)
         dg = deng.capture(advance=False)
@@ -370,6 +375,7 @@ def main():
             "data": "synthetic: random-init weights N(0,0.02), KV cache N(0,0.02) (reference fixed-context protocol)",
             "config": {"workload": workload, "model": args.model, "nm": args.nm, "ctx": args.ctx,
                        "parallelism": f"tp{world}", "prefetch": args.prefetch, "next_prefetch": args.next_prefetch,
+                       "executor": engine_mode,
                        "l2": "no flush: every replay streams all weights (>> 126 MB L2)"},
             "e2e": {"value": round(e2e_ms, 4), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
                     "steps": e2e_steps, "note": "public generation API, host token in/out every step"},

@@ -152,6 +152,11 @@ typedef struct nms_gemv_fused_args {
   const void* next_prefetch[2];
   int64_t next_prefetch_bytes[2];
   int64_t next_prefetch_head;
+  /* Token-indexed input (optional): x is a [x_rows, K] table and the GEMV
+   * input is its row *x_token, read on the device -- the token embedding
+   * (model.py:164) folded into the first GEMV of a decode step. */
+  const int64_t* x_token;
+  int64_t x_rows;
 } nms_gemv_fused_args;
 
 int nms_gemv_fused_f16(const nms_gemv_fused_args* args, void* stream);
@@ -233,6 +238,32 @@ int nms_plan_add_embedding(nms_plan* plan, const void* table, const int64_t* tok
 int nms_plan_size(const nms_plan* plan, int32_t* out);
 /* Launch records [begin, end) on `stream`. */
 int nms_plan_launch(const nms_plan* plan, int32_t begin, int32_t end, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Persistent decode step: the GEMV and attention records listed in
+ * `records` (plan indices, in execution order) run as stages of ONE
+ * cooperative kernel (one 1024-thread CTA per SM) separated by in-kernel grid
+ * barriers; each CTA issues the next GEMV stage's first weight loads before
+ * it waits at a barrier.  Replaces the per-kernel decode step of the plan
+ * (and, like it, the reference's compiled + graph-captured decode_one_token).
+ * Records other than GEMV and attention (embedding, pack) return
+ * NMS_ERR_NOT_IMPLEMENTED, and the plan path is used.  nms_step_create
+ * allocates the stage table and barrier/attention scratch once (device
+ * memory, freed by nms_step_destroy); launches allocate nothing.  Barrier
+ * waits are bounded (device error 3 on timeout).
+ * ------------------------------------------------------------------------- */
+typedef struct nms_step nms_step;
+
+int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecords, nms_step** out);
+int nms_step_launch(const nms_step* step, void* stream);
+int nms_step_destroy(nms_step* step);
+/* Stage count and CTAs of a persistent step. */
+int nms_step_info(const nms_step* step, int32_t* nstages, int32_t* grid);
+/* Optional timeline of later launches (NULL disables), in %globaltimer ns:
+ * buf[0] = kernel start; buf[1 + s*(grid+1) + c] = when CTA c finished the
+ * work of stage s; buf[1 + s*(grid+1) + grid] = when CTA 0 left the barrier
+ * after stage s.  Needs 1 + nstages*(grid+1) uint64 entries (device memory). */
+int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity);
 
 #ifdef __cplusplus
 }

@@ -56,6 +56,11 @@ EXPORTED_SYMBOLS = (
     "nms_plan_add_embedding",
     "nms_plan_size",
     "nms_plan_launch",
+    "nms_step_create",
+    "nms_step_launch",
+    "nms_step_destroy",
+    "nms_step_info",
+    "nms_step_set_trace",
 )
 
 c_void_p = ctypes.c_void_p
@@ -99,6 +104,8 @@ class NmsGemvFusedArgs(ctypes.Structure):
         ("next_prefetch", c_void_p * 2),
         ("next_prefetch_bytes", c_i64 * 2),
         ("next_prefetch_head", c_i64),
+        ("x_token", c_void_p),
+        ("x_rows", c_i64),
     ]
 
 
@@ -154,6 +161,11 @@ def _declare(lib: ctypes.CDLL) -> None:
         "nms_plan_add_embedding": (I32, [P, P, P, P, I64, I64, I32]),
         "nms_plan_size": (I32, [P, ctypes.POINTER(I32)]),
         "nms_plan_launch": (I32, [P, I32, I32, P]),
+        "nms_step_create": (I32, [P, ctypes.POINTER(I32), I32, ctypes.POINTER(P)]),
+        "nms_step_launch": (I32, [P, P]),
+        "nms_step_destroy": (I32, [P]),
+        "nms_step_info": (I32, [P, ctypes.POINTER(I32), ctypes.POINTER(I32)]),
+        "nms_step_set_trace": (I32, [P, P, I64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

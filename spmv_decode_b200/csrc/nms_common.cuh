@@ -22,6 +22,7 @@ enum DeviceError : int {
   kDevOk = 0,
   kDevBulkCopyTimeout = 1,   // mbarrier wait on a bulk copy ran past its limit
   kDevBadPosition = 2,       // attention: token position outside the KV cache
+  kDevBarrierTimeout = 3,    // persistent step: a grid barrier wait ran past its limit
 };
 __device__ int g_device_error;
 

@@ -64,7 +64,9 @@ struct GemvParams {
   const char* next_pf[2];  // weights of the next launch (see prefetch_shares_l2)
   uint32_t next_pf_bytes[2];
   uint32_t next_pf_head;
-  const __half* x;
+  const __half* x;          // input vector, or a [x_rows, K] table when x_token is set
+  const int64_t* x_token;   // optional: the input is row *x_token of the table x (embedding)
+  int64_t x_rows;
   const __half* x2;
   const __half* norm_w;
   float eps;
@@ -117,6 +119,16 @@ __host__ __device__ inline size_t gemv_smem_bytes(int K, int w, int w_pad, int n
   return off;
 }
 
+// The GEMV input vector: p.x, or row *p.x_token of the table p.x (the token
+// embedding folded into the first GEMV of a decode step).  Must be called
+// after the dependency wait (the token is produced by the previous step).
+__device__ __forceinline__ const __half* input_row(const GemvParams& p) {
+  if (p.x_token == nullptr) return p.x;
+  int64_t t = *p.x_token;
+  if (t < 0 || t >= p.x_rows) t = 0;  // host validates the ids it supplies
+  return p.x + (size_t)t * p.K;
+}
+
 // Row owned by this lane's subgroup for virtual row-group `vg` of the CTA.
 struct LaneRow {
   int segi;   // segment
@@ -147,7 +159,8 @@ __device__ __forceinline__ LaneRow lane_row(const GemvParams& p, bool paired, in
 // Epilogue over a CTA's rows [g0*RG, g0*RG + ng*RG): store, SwiGLU or
 // store + grid-wide argmax (last CTA reduces the per-CTA partials).
 template <int NT>
-__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* acc, int g0, int ng, int RG) {
+__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* acc, int g0, int ng, int RG,
+                                              unsigned cta, unsigned ncta) {
   constexpr int NWE = NT / kWarp;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* s_acc = acc;
@@ -199,11 +212,11 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
           bi = si[q];
         }
       }
-      p.amax_val[blockIdx.x] = bv;
-      p.amax_idx[blockIdx.x] = bi;
+      p.amax_val[cta] = bv;
+      p.amax_idx[cta] = bi;
       __threadfence();
       const uint32_t prev = atomicAdd(p.amax_counter, 1u);
-      s_last = (prev == gridDim.x - 1) ? 1 : 0;
+      s_last = (prev == ncta - 1) ? 1 : 0;
     }
     __syncthreads();
     if (s_last) {
@@ -212,7 +225,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
       __threadfence();
       float fv = -INFINITY;
       int fi = 0x7fffffff;
-      for (int q = tid; q < (int)gridDim.x; q += NT) {
+      for (int q = tid; q < (int)ncta; q += NT) {
         const float qv = __ldcg(p.amax_val + q);
         const int qi = __ldcg(p.amax_idx + q);
         if (qv > fv || (qv == fv && qi < fi)) {
@@ -387,20 +400,21 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_packed_kernel(const __gr
   grid_dep_wait();
 
   // --- 3. Stage x in shared memory.
+  const __half* xsrc = input_row(p);
   float rstd = 1.f;
   if (x_bulk) {
     if (tid == 0) {
       mbar_arrive_expect_tx(&s.bar[1], (uint32_t)p.K * 2);
-      bulk_copy_g2s(s.xs, p.x, (uint32_t)p.K * 2, &s.bar[1]);
+      bulk_copy_g2s(s.xs, xsrc, (uint32_t)p.K * 2, &s.bar[1]);
     }
   } else {
     float ss = 0.f;
-    const bool vec = ((p.K & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0) &&
+    const bool vec = ((p.K & 7) == 0) && ((reinterpret_cast<uintptr_t>(xsrc) & 15u) == 0) &&
                      (p.x2 == nullptr || (reinterpret_cast<uintptr_t>(p.x2) & 15u) == 0);
     if (vec) {
       // 16-byte pieces: one load of x (and x2) per thread for K <= 4096.
       for (int i8 = tid; i8 < p.K / 8; i8 += kGemvThreads) {
-        const uint4 a = *reinterpret_cast<const uint4*>(p.x + (size_t)i8 * 8);
+        const uint4 a = *reinterpret_cast<const uint4*>(xsrc + (size_t)i8 * 8);
         uint4 b = make_uint4(0u, 0u, 0u, 0u);
         const bool add = (p.prologue == kProResidNorm && p.x2 != nullptr);
         if (add) b = *reinterpret_cast<const uint4*>(p.x2 + (size_t)i8 * 8);
@@ -419,7 +433,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_packed_kernel(const __gr
       }
     } else {
       for (int i = tid; i < p.K; i += kGemvThreads) {
-        float v = h2f(p.x[i]);
+        float v = h2f(xsrc[i]);
         if (p.prologue == kProResidNorm && p.x2 != nullptr) v = h2f(f2h(v + h2f(p.x2[i])));
         const __half hv = f2h(v);
         s.xs[i] = hv;
@@ -543,7 +557,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_packed_kernel(const __gr
   __syncthreads();
 
   // --- 6. Epilogue over this CTA's rows.
-  gemv_epilogue<kGemvThreads>(p, s.acc, g0, ng, RG);
+  gemv_epilogue<kGemvThreads>(p, s.acc, g0, ng, RG, blockIdx.x, gridDim.x);
 }
 
 // ---------------------------------------------------------------------------

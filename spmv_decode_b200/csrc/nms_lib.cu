@@ -26,6 +26,7 @@
 #include "nms_common.cuh"
 #include "nms_decode.cuh"
 #include "nms_gemv.cuh"
+#include "nms_step.cuh"
 
 namespace {
 
@@ -54,6 +55,7 @@ struct DeviceInfo {
   bool ready = false;
   int num_sms = 0;
   size_t max_smem_optin = 0;
+  size_t step_smem_max = 0;
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -94,6 +96,15 @@ int device_info(const DeviceInfo** out) {
     }
     // Dynamic shared memory available to every kernel that takes it.
     d.max_smem_optin = (size_t)smem - static_max;
+    {
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, (const void*)nms::decode_step_kernel);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncGetAttributes(decode_step_kernel)");
+      e = cudaFuncSetAttribute((const void*)nms::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem - (int)fa.sharedSizeBytes);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(decode_step_kernel)");
+      d.step_smem_max = (size_t)smem - fa.sharedSizeBytes;
+    }
     e = cudaFuncSetAttribute((const void*)nms::attention_decode_kernel,
                              cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(NonPortableClusterSizeAllowed)");
@@ -104,15 +115,20 @@ int device_info(const DeviceInfo** out) {
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
-                      dim3 cluster, Args&&... args) {
+cudaError_t launch_ex2(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                       dim3 cluster, bool cooperative, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attrs[2];
+  cudaLaunchAttribute attrs[3];
   int na = 0;
+  if (cooperative) {
+    attrs[na].id = cudaLaunchAttributeCooperative;
+    attrs[na].val.cooperative = 1;
+    ++na;
+  }
   if (pdl) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
@@ -128,6 +144,12 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
   cfg.attrs = attrs;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                      dim3 cluster, Args&&... args) {
+  return launch_ex2(kernel, grid, block, smem, st, pdl, cluster, false, std::forward<Args>(args)...);
 }
 
 struct EmbedParams {
@@ -319,6 +341,9 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
   p.amax_idx = a->amax_idx;
   p.amax_counter = a->amax_counter;
   p.token_out = a->token_out;
+  p.x_token = a->x_token;
+  p.x_rows = a->x_rows;
+  if (a->x_token != nullptr && a->x_rows <= 0) return fail(NMS_ERR_VALUE, "x_token needs x_rows > 0");
   p.next_token = a->next_token;
   p.token_history = a->token_history;
   p.pos = a->pos;
@@ -448,6 +473,15 @@ int noalloc_scratch(unsigned char** out) {
 
 struct nms_plan {
   std::vector<LaunchRec> recs;
+};
+
+struct nms_step {
+  int device = 0;
+  int nstages = 0;
+  int grid = 0;
+  size_t smem = 0;
+  void* dev_mem = nullptr;  // stages | barrier words | attention partials | head counters
+  nms::StepParams params;
 };
 
 extern "C" {
@@ -707,6 +741,122 @@ int nms_plan_add_embedding(nms_plan* plan, const void* table, const int64_t* tok
 int nms_plan_size(const nms_plan* plan, int32_t* out) {
   if (plan == nullptr || out == nullptr) return fail(NMS_ERR_VALUE, "null argument");
   *out = (int32_t)plan->recs.size();
+  return NMS_OK;
+}
+
+int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecords, nms_step** out) {
+  if (plan == nullptr || out == nullptr || records == nullptr) return fail(NMS_ERR_VALUE, "null argument");
+  const int32_t n = (int32_t)plan->recs.size();
+  if (nrecords < 1) return fail(NMS_ERR_VALUE, "no records");
+  for (int32_t k = 0; k < nrecords; ++k)
+    if (records[k] < 0 || records[k] >= n) return fail(NMS_ERR_VALUE, "record %d outside plan of %d", records[k], n);
+  const DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const int grid = dev->num_sms;
+  std::vector<nms::StepStage> stages;
+  size_t smem = sizeof(nms::StepAttnSmem);
+  int max_units = 0, max_hkv = 0;
+  for (int32_t k = 0; k < nrecords; ++k) {
+    const int32_t i = records[k];
+    const LaunchRec& r = plan->recs[i];
+    nms::StepStage st;
+    memset(&st, 0, sizeof(st));
+    if (r.kind == LaunchRec::kGemvPacked) {
+      st.kind = nms::kStageGemv;
+      st.lanes = r.lanes;
+      st.g = r.gp;
+      if (st.g.epilogue == nms::kEpiArgmax && st.g.amax_val == nullptr)
+        return fail(NMS_ERR_VALUE, "record %d: argmax without scratch", i);
+      const bool paired = st.g.mode == nms::kModePaired;
+      const int nsegx = paired ? 2 : st.g.nseg;
+      const int max_vrows = (paired ? 2 : 1) * ((st.g.row_groups + grid - 1) / grid);
+      const size_t need = nms::gemv_smem_bytes(st.g.K, st.g.w, st.g.w_pad, nsegx, max_vrows);
+      if (need > smem) smem = need;
+    } else if (r.kind == LaunchRec::kAttention) {
+      if (r.ap.splits > nms::kMaxSplits)
+        return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: %d attention splits (max %d)", i, r.ap.splits, nms::kMaxSplits);
+      st.kind = nms::kStageAttn;
+      st.a = r.ap;
+      st.units = st.a.Hkv * st.a.splits;
+      if (st.units > max_units) max_units = st.units;
+      if (st.a.Hkv > max_hkv) max_hkv = st.a.Hkv;
+    } else {
+      return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: only GEMV and attention launches run in a persistent step", i);
+    }
+    stages.push_back(st);
+  }
+  if (smem > dev->step_smem_max)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "persistent step needs %zu bytes of shared memory (limit %zu)", smem,
+                dev->step_smem_max);
+  const size_t stage_bytes = stages.size() * sizeof(nms::StepStage);
+  const size_t bar_off = nms::align_up_sz(stage_bytes, 256);
+  const size_t part_off = bar_off + 256;
+  const size_t part_bytes = (size_t)max_units * nms::kAttnMaxGroup * (nms::kAttnD + 2) * sizeof(float);
+  const size_t cnt_off = nms::align_up_sz(part_off + part_bytes, 256);
+  const size_t total = cnt_off + nms::align_up_sz((size_t)(max_hkv > 0 ? max_hkv : 1) * sizeof(unsigned), 256);
+  nms_step* st = new (std::nothrow) nms_step();
+  if (st == nullptr) return fail(NMS_ERR_CUDA, "out of host memory");
+  cudaError_t e = cudaGetDevice(&st->device);
+  if (e == cudaSuccess) e = cudaMalloc(&st->dev_mem, total);
+  if (e == cudaSuccess) e = cudaMemset(st->dev_mem, 0, total);
+  if (e == cudaSuccess) e = cudaMemcpy(st->dev_mem, stages.data(), stage_bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    if (st->dev_mem) cudaFree(st->dev_mem);
+    delete st;
+    return fail_cuda(e, "persistent step set-up");
+  }
+  unsigned char* base = static_cast<unsigned char*>(st->dev_mem);
+  st->nstages = (int)stages.size();
+  st->grid = grid;
+  st->smem = smem;
+  st->params.stages = reinterpret_cast<const nms::StepStage*>(base);
+  st->params.nstages = st->nstages;
+  st->params.bar_count = reinterpret_cast<unsigned*>(base + bar_off);
+  st->params.bar_exit = reinterpret_cast<unsigned*>(base + bar_off + 128);
+  st->params.attn_part = reinterpret_cast<float*>(base + part_off);
+  st->params.attn_count = reinterpret_cast<unsigned*>(base + cnt_off);
+  st->params.trace = nullptr;
+  *out = st;
+  return NMS_OK;
+}
+
+int nms_step_launch(const nms_step* step, void* stream) {
+  if (step == nullptr) return fail(NMS_ERR_VALUE, "step is null");
+  cudaError_t e = launch_ex2(nms::decode_step_kernel, dim3(step->grid), dim3(nms::kStepThreads), step->smem,
+                             static_cast<cudaStream_t>(stream), false, dim3(1, 1, 1), true, step->params);
+  if (e != cudaSuccess) return fail_cuda(e, "decode_step_kernel launch");
+  return NMS_OK;
+}
+
+int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity) {
+  if (step == nullptr) return fail(NMS_ERR_VALUE, "step is null");
+  if (buffer == nullptr) {
+    step->params.trace = nullptr;
+    return NMS_OK;
+  }
+  const int64_t need = 1 + (int64_t)step->nstages * (step->grid + 1);
+  if (capacity < need) return fail(NMS_ERR_VALUE, "trace needs %lld entries, got %lld", (long long)need, (long long)capacity);
+  if (!aligned(buffer, 8)) return fail(NMS_ERR_VALUE, "trace buffer must be 8-byte aligned");
+  step->params.trace = static_cast<unsigned long long*>(buffer);
+  return NMS_OK;
+}
+
+int nms_step_info(const nms_step* step, int32_t* nstages, int32_t* grid) {
+  if (step == nullptr || nstages == nullptr || grid == nullptr) return fail(NMS_ERR_VALUE, "null argument");
+  *nstages = step->nstages;
+  *grid = step->grid;
+  return NMS_OK;
+}
+
+int nms_step_destroy(nms_step* step) {
+  if (step == nullptr) return NMS_OK;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(step->device);
+  if (step->dev_mem) cudaFree(step->dev_mem);
+  cudaSetDevice(cur);
+  delete step;
   return NMS_OK;
 }
 

@@ -57,7 +57,7 @@ class DecodeEngine:
     """Batch-1 decode state + native plan for one model on one device."""
 
     def __init__(self, model: Transformer, max_seq_length: int, *, pdl: bool = True, prefetch_bytes: int = 0,
-                 next_prefetch_bytes: int = 0, attn_splits: int = 0, history_len: int = 0,
+                 next_prefetch_bytes: int = 0, attn_splits: int = 0, history_len: int = 0, mode: str = "auto",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None, tp_rank: int = 0, tp_size: int = 1,
                  local_heads: Optional[tuple] = None):
         c = model.config
@@ -71,6 +71,8 @@ class DecodeEngine:
         self.prefetch_bytes = int(prefetch_bytes)  # per-warp L2 look-ahead inside a GEMV
         self.next_prefetch_bytes = int(next_prefetch_bytes)  # L2 prefetch of the following GEMV's weights
         self.allreduce = allreduce
+        if mode not in ("auto", "persistent", "plan"):
+            raise ValueError(f"unknown mode {mode!r}")
         self.tp_rank, self.tp_size = tp_rank, tp_size
         Hq, Hkv = local_heads if local_heads is not None else (c.n_head, c.n_local_heads)
         self.Hq, self.Hkv, self.D = Hq, Hkv, c.head_dim
@@ -117,6 +119,23 @@ class DecodeEngine:
             self.gemv_records: List[dict] = []
             self._pending: List[tuple] = []  # launches in step order, added to the plan by _finalize
             self._build(model, attn_splits)
+            self._steps = {}
+            self.mode = "plan"
+            if mode != "plan" and allreduce is None:
+                try:
+                    fixed = list(range(self._head_index)) + [self._head_index]
+                    adv = list(range(self._head_index)) + [self._head_index + 1]
+                    for key, recs in ((False, fixed), (True, adv)):
+                        arr = (ctypes.c_int32 * len(recs))(*recs)
+                        h = ctypes.c_void_p()
+                        _lib.check(_lib.lib().nms_step_create(self._plan, arr, len(recs), ctypes.byref(h)),
+                                   "nms_step_create")
+                        self._steps[key] = h
+                    self.mode = "persistent"
+                except NotImplementedError:
+                    if mode == "persistent":
+                        raise
+                    self._destroy_steps()
 
     # ------------------------------------------------------------------ build
     def _h(self, t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -130,7 +149,7 @@ class DecodeEngine:
         return (_lib.NMS_FLAG_PDL if self.pdl else 0) | (_lib.NMS_FLAG_DENSE if dense else 0)
 
     def _add_gemv(self, linears, *, x, out, x2=None, norm=None, eps=0.0, resid_out=None, swiglu=False,
-                  argmax=False, advance=False):
+                  argmax=False, advance=False, x_token=None):
         segs = [_linear_segment(l) for l in linears]
         s0 = segs[0]
         for s in segs[1:]:
@@ -149,6 +168,9 @@ class DecodeEngine:
         a.K, a.w, a.w_pad = s0["K"], s0["w"], s0["w_pad"]
         a.block_width, a.vec_width = s0["n"], s0["m"]
         a.x = x.data_ptr()
+        if x_token is not None:  # x is a table; the input is row *x_token
+            a.x_token = x_token.data_ptr()
+            a.x_rows = x.shape[0]
         a.x2 = None if x2 is None else x2.data_ptr()
         a.norm_weight = None if norm is None else norm.data_ptr()
         a.eps = float(eps)
@@ -196,13 +218,14 @@ class DecodeEngine:
         if emb.dtype != torch.float16:
             raise TypeError("model must be float16 (the reference decode path is fp16)")
         self.emb = emb
-        self._pending.append(("emb", (emb.data_ptr(), self.token_in.data_ptr(), self.x_emb.data_ptr(), c.dim,
-                                      emb.shape[0], self._flags()), None))
+        # The token embedding is folded into the first q/k/v GEMV's prologue
+        # (input = row token_in of the embedding table).
         for li, blk in enumerate(model.layers):
             attn, ffn = blk.attn, blk.ffn
             qkv_lins = [attn.wqkv] if c.attn_layout == "fused" else [attn.q_proj, attn.k_proj, attn.v_proj]
-            self._add_gemv(qkv_lins, x=self.x_emb if li == 0 else self.h_buf, x2=None if li == 0 else self.y_down,
-                           norm=self._h(blk.norm1.weight), eps=blk.norm1.eps, resid_out=self.x_buf, out=self.qkv)
+            self._add_gemv(qkv_lins, x=emb if li == 0 else self.h_buf, x2=None if li == 0 else self.y_down,
+                           norm=self._h(blk.norm1.weight), eps=blk.norm1.eps, resid_out=self.x_buf, out=self.qkv,
+                           x_token=self.token_in if li == 0 else None)
             aa = _lib.NmsAttentionArgs()
             aa.qkv = self.qkv.data_ptr()
             aa.k_cache = self.k_cache[li].data_ptr()
@@ -286,6 +309,9 @@ class DecodeEngine:
         writes logits and token_out (and with ``advance`` also token_in,
         history[pos] and pos += 1)."""
         stream = stream or torch.cuda.current_stream(self.device)
+        if self.mode == "persistent":
+            _lib.check(_lib.lib().nms_step_launch(self._steps[advance], stream.cuda_stream), "nms_step_launch")
+            return
         begin = 0
         if self.allreduce is not None:
             # Cut points alternate: after the o-projection (partial y_o) and
@@ -332,7 +358,45 @@ class DecodeEngine:
         torch.cuda.synchronize(self.device)
         return g
 
+    def step_timeline(self, advance: bool = False, warmup: int = 2) -> dict:
+        """Run the persistent step once with its timeline enabled and return
+        per-stage statistics in microseconds: work (previous barrier release to
+        the slowest CTA's finish), imbalance (slowest - fastest CTA finish) and
+        barrier (slowest finish to release)."""
+        if self.mode != "persistent":
+            raise RuntimeError("the timeline needs the persistent executor")
+        L = _lib.lib()
+        h = self._steps[advance]
+        ns, grid = ctypes.c_int32(), ctypes.c_int32()
+        _lib.check(L.nms_step_info(h, ctypes.byref(ns), ctypes.byref(grid)))
+        n, g = int(ns.value), int(grid.value)
+        buf = torch.zeros(1 + n * (g + 1), dtype=torch.int64, device=self.device)
+        for _ in range(warmup):
+            self.step(advance=advance)
+        _lib.check(L.nms_step_set_trace(h, buf.data_ptr(), buf.numel()))
+        self.step(advance=advance)
+        torch.cuda.synchronize(self.device)
+        _lib.check(L.nms_step_set_trace(h, None, 0))
+        t = buf.cpu().double()
+        t0 = t[0].item()
+        rows = t[1:].view(n, g + 1)
+        stages = []
+        prev = t0
+        for s in range(n):
+            fin = rows[s, :g]
+            rel = rows[s, g].item() if s + 1 < n else fin.max().item()
+            stages.append({"work_us": (fin.max().item() - prev) / 1e3, "imbalance_us": (fin.max() - fin.min()).item() / 1e3,
+                           "barrier_us": (rel - fin.max().item()) / 1e3})
+            prev = rel
+        return {"total_us": (prev - t0) / 1e3, "stages": stages}
+
+    def _destroy_steps(self) -> None:
+        for h in getattr(self, "_steps", {}).values():
+            _lib.lib().nms_step_destroy(h)
+        self._steps = {}
+
     def close(self) -> None:
+        self._destroy_steps()
         if self._plan:
             _lib.lib().nms_plan_destroy(self._plan)
             self._plan = ctypes.c_void_p()

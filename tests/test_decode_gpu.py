@@ -61,12 +61,18 @@ def _model_from_golden(z, kind, dev):
     return model, prompt_len, steps
 
 
+MODES = ["persistent", "plan"]
+
+
+@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("kind", ["llama", "qwen3"])
-def test_reference_fixture_decode(cuda_device, kind):
-    """The reference decode path's own tokens and logits (tests/golden)."""
+def test_reference_fixture_decode(cuda_device, kind, mode):
+    """The reference decode path's own tokens and logits (tests/golden),
+    with both decode-step executors."""
     z = np.load(GOLDEN / f"decode_{kind}_tiny.npz")
     model, prompt_len, steps = _model_from_golden(z, kind, cuda_device)
-    eng = DecodeEngine(model, 64, history_len=64)
+    eng = DecodeEngine(model, 64, history_len=64, mode=mode)
+    assert eng.mode == mode
     toks, logits = GraphDecoder(eng).run(z["prompt"].tolist(), steps + 1, keep_logits=True)
     ref = _f16(z["logits"]).float()
     got = logits.float().cpu()
@@ -108,37 +114,40 @@ def _teacher_forced_check(eng, om, prompt, steps):
     return toks, agree, ties, worst
 
 
-def test_qwen3_06b_architecture_vs_oracle(cuda_device):
+@pytest.mark.parametrize("mode", MODES)
+def test_qwen3_06b_architecture_vs_oracle(cuda_device, mode):
     """BASELINE config 3 shapes (28 layers, hidden 1024, 16/8 heads, head_dim
     128, SwiGLU 3072, tied 151936 vocab), 32:64, reference-bit-exact packer;
     prompt of 128 seeded random ids, 64 greedy steps."""
     model = build_model("qwen3-0.6b", nm=(32, 64), device=cuda_device, seed=11, init="reference")
     prompt = torch.randint(0, 151936, (128,), generator=torch.Generator().manual_seed(5)).tolist()
-    eng = DecodeEngine(model, 256, history_len=256)
+    eng = DecodeEngine(model, 256, history_len=256, mode=mode)
     om = OracleModel.from_transformer(model, max_seq=256)
     toks, agree, ties, worst = _teacher_forced_check(eng, om, prompt, 64)
     assert len(toks) == 64 and agree + ties == 64 and agree >= 60
     eng.close()
 
 
-def test_llama31_8b_width_vs_oracle(cuda_device):
+@pytest.mark.parametrize("mode", MODES)
+def test_llama31_8b_width_vs_oracle(cuda_device, mode):
     """Llama-3.1-8B widths (hidden 4096, 32/8 heads, SwiGLU 14336, untied 128256
     head, RoPE theta 5e5 with 3.1 scaling) at 2 layers, 32:64; 64 greedy steps."""
     args = ModelArgs.from_name("llama-3.1-8b")
     args.n_layer = 2
     model = build_model(args, nm=(32, 64), device=cuda_device, seed=3, init="reference")
     prompt = torch.randint(0, 128256, (16,), generator=torch.Generator().manual_seed(6)).tolist()
-    eng = DecodeEngine(model, 128, history_len=128)
+    eng = DecodeEngine(model, 128, history_len=128, mode=mode)
     om = OracleModel.from_transformer(model, max_seq=128)
     toks, agree, ties, worst = _teacher_forced_check(eng, om, prompt, 64)
     assert agree + ties == 64 and agree >= 60
     eng.close()
 
 
-def test_eager_step_equals_graph_replay(cuda_device):
+@pytest.mark.parametrize("mode", MODES)
+def test_eager_step_equals_graph_replay(cuda_device, mode):
     model = build_model(ModelArgs(block_size=64, vocab_size=1024, n_layer=2, n_head=4, n_local_heads=2, dim=512,
                                   intermediate_size=1024), nm=(8, 16), device=cuda_device, seed=1)
-    eng = DecodeEngine(model, 64, history_len=64)
+    eng = DecodeEngine(model, 64, history_len=64, mode=mode)
     eager = []
     tok = 5
     for pos in range(12):
@@ -171,12 +180,24 @@ def test_fixed_context_protocol_is_repeatable(cuda_device):
     eng.close()
 
 
-def test_dense_linears_engine(cuda_device):
+@pytest.mark.parametrize("mode", MODES)
+def test_dense_linears_engine(cuda_device, mode):
     """The same engine with dense linears (the dense control) matches the oracle."""
     model = build_model(ModelArgs(block_size=64, vocab_size=1024, n_layer=2, n_head=4, n_local_heads=2, dim=512,
                                   intermediate_size=1024), nm=None, device=cuda_device, seed=4)
-    eng = DecodeEngine(model, 64, history_len=64)
+    eng = DecodeEngine(model, 64, history_len=64, mode=mode)
     om = OracleModel.from_transformer(model, max_seq=64)
     toks, agree, ties, worst = _teacher_forced_check(eng, om, [1, 2, 3], 16)
     assert agree + ties == 16 and agree >= 15
+    eng.close()
+
+
+
+def test_auto_mode_is_persistent(cuda_device):
+    """Mixed packed widths (lanes per row 8 and 16 in one step) run in the
+    persistent kernel."""
+    model = build_model(ModelArgs(block_size=64, vocab_size=512, n_layer=1, n_head=2, n_local_heads=1, dim=256,
+                                  intermediate_size=384), nm=(16, 32), device=cuda_device, seed=5)
+    eng = DecodeEngine(model, 32, history_len=32, mode="auto")
+    assert eng.mode == "persistent"
     eng.close()
