@@ -49,8 +49,10 @@ const char* nms_status_name(int status);
 int nms_num_sms(int* out);
 /* Reads the device error word that kernels set instead of faulting or
  * hanging (1 = bulk-copy wait timed out, 2 = attention position outside the
- * KV cache; the kernel skipped its work).  Synchronizes the current device.  With
- * clear != 0 the word is reset to 0. */
+ * KV cache, 3 = persistent-step grid barrier timed out, 4 = persistent-step
+ * weight-ring slot never refilled, 5 = persistent-step weight-ring chunk does
+ * not fit its stage; the kernel skipped its work).  Synchronizes the current
+ * device.  With clear != 0 the word is reset to 0. */
 int nms_device_error(int* code_out, int clear);
 
 /* ---------------------------------------------------------------------------

@@ -23,6 +23,8 @@ enum DeviceError : int {
   kDevBulkCopyTimeout = 1,   // mbarrier wait on a bulk copy ran past its limit
   kDevBadPosition = 2,       // attention: token position outside the KV cache
   kDevBarrierTimeout = 3,    // persistent step: a grid barrier wait ran past its limit
+  kDevRingTimeout = 4,       // persistent step: a weight-ring slot was never refilled
+  kDevRingMismatch = 5,      // persistent step: a weight-ring chunk does not fit its stage
 };
 __device__ int g_device_error;
 
@@ -171,20 +173,25 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // time, records kDevBulkCopyTimeout and returns false.  A bulk copy moves a
 // few tens of KB, so the limit (hundreds of ms) is only reached if the copy
 // engine has failed.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   uint64_t limit_ns) {
   const uint32_t addr = smem_u32(bar);
-  uint32_t done = 0;
+  if (mbar_try_wait(addr, parity)) return true;  // common case: no timer read
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_try_wait(addr, parity)) return true;
     if (global_timer_ns() - t0 > limit_ns) {
       set_device_error(kDevBulkCopyTimeout);
       return false;

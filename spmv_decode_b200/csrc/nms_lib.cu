@@ -14,6 +14,7 @@
 // replays them (nms_plan_launch), which is the decode-step executor.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -23,6 +24,7 @@
 #include <vector>
 
 #include "../../include/nmsparse_b200.h"
+
 #include "nms_common.cuh"
 #include "nms_decode.cuh"
 #include "nms_gemv.cuh"
@@ -96,14 +98,15 @@ int device_info(const DeviceInfo** out) {
     }
     // Dynamic shared memory available to every kernel that takes it.
     d.max_smem_optin = (size_t)smem - static_max;
-    {
+    d.step_smem_max = (size_t)smem;
+    for (const void* k : {(const void*)nms::decode_step_kernel<nms::kStepDepthHi>,
+                          (const void*)nms::decode_step_kernel<nms::kStepDepthLo>}) {
       cudaFuncAttributes fa;
-      e = cudaFuncGetAttributes(&fa, (const void*)nms::decode_step_kernel);
+      e = cudaFuncGetAttributes(&fa, k);
       if (e != cudaSuccess) return fail_cuda(e, "cudaFuncGetAttributes(decode_step_kernel)");
-      e = cudaFuncSetAttribute((const void*)nms::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem - (int)fa.sharedSizeBytes);
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem - (int)fa.sharedSizeBytes);
       if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(decode_step_kernel)");
-      d.step_smem_max = (size_t)smem - fa.sharedSizeBytes;
+      d.step_smem_max = std::min(d.step_smem_max, (size_t)smem - fa.sharedSizeBytes);
     }
     e = cudaFuncSetAttribute((const void*)nms::attention_decode_kernel,
                              cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -164,6 +167,7 @@ struct EmbedParams {
 struct LaunchRec {
   enum Kind { kGemvPacked, kGemvRef, kAttention, kEmbedding, kPack, kUnpack } kind;
   int lanes = 0;  // gemv_packed_kernel template argument
+  int amax_capacity = 0;  // argmax epilogue: partials the caller's scratch holds
   nms::GemvParams gp;
   nms::GemvRefParams rp;
   nms::AttnParams ap;
@@ -364,6 +368,7 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
                 (long long)K, (long long)w_pad, nsegx, smem, dev->max_smem_optin);
   rec->kind = LaunchRec::kGemvPacked;
   rec->lanes = L;
+  rec->amax_capacity = (epi == nms::kEpiArgmax) ? a->amax_capacity : 0;
   rec->grid = dim3(grid);
   rec->block = dim3(nms::kGemvThreads);
   rec->smem = smem;
@@ -480,7 +485,8 @@ struct nms_step {
   int nstages = 0;
   int grid = 0;
   size_t smem = 0;
-  void* dev_mem = nullptr;  // stages | barrier words | attention partials | head counters
+  int depth = 0;            // weight-ring depth (selects the kernel instantiation)
+  void* dev_mem = nullptr;  // stage tables | barrier words | attention partials | head counters
   nms::StepParams params;
 };
 
@@ -754,43 +760,79 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
   int rc = device_info(&dev);
   if (rc) return rc;
   const int grid = dev->num_sms;
-  std::vector<nms::StepStage> stages;
-  size_t smem = sizeof(nms::StepAttnSmem);
+  std::vector<int32_t> kinds;
+  std::vector<nms::StepGemv> gemvs;
+  std::vector<nms::ProdDesc> descs;
+  std::vector<nms::AttnParams> attns;
+  size_t act = sizeof(nms::StepAttnSmem);
   int max_units = 0, max_hkv = 0;
+  const int64_t* pos_ptr = nullptr;
   for (int32_t k = 0; k < nrecords; ++k) {
     const int32_t i = records[k];
     const LaunchRec& r = plan->recs[i];
-    nms::StepStage st;
-    memset(&st, 0, sizeof(st));
     if (r.kind == LaunchRec::kGemvPacked) {
-      st.kind = nms::kStageGemv;
-      st.lanes = r.lanes;
-      st.g = r.gp;
-      if (st.g.epilogue == nms::kEpiArgmax && st.g.amax_val == nullptr)
-        return fail(NMS_ERR_VALUE, "record %d: argmax without scratch", i);
-      const bool paired = st.g.mode == nms::kModePaired;
-      const int nsegx = paired ? 2 : st.g.nseg;
-      const int max_vrows = (paired ? 2 : 1) * ((st.g.row_groups + grid - 1) / grid);
-      const size_t need = nms::gemv_smem_bytes(st.g.K, st.g.w, st.g.w_pad, nsegx, max_vrows);
-      if (need > smem) smem = need;
+      nms::StepGemv sg;
+      memset(&sg, 0, sizeof(sg));
+      sg.g = r.gp;
+      sg.lanes = nms::ring_lanes(sg.g.w_pad);
+      const int RG = 32 / sg.lanes;
+      sg.g.row_groups = (sg.g.rows_total + RG - 1) / RG;
+      if (sg.g.epilogue == nms::kEpiArgmax && (sg.g.amax_val == nullptr || grid > r.amax_capacity))
+        return fail(NMS_ERR_VALUE, "record %d: argmax scratch holds %d partials, the step needs %d", i,
+                    r.amax_capacity, grid);
+      const bool paired = sg.g.mode == nms::kModePaired;
+      const int nsegx = paired ? 2 : sg.g.nseg;
+      const int max_vrows = (paired ? 2 : 1) * ((sg.g.row_groups + grid - 1) / grid) * RG;
+      const size_t need = nms::step_gemv_smem_bytes(sg.g.K, sg.g.w, sg.g.w_pad, nsegx, max_vrows,
+                                                    sg.g.prologue == nms::kProResidNorm);
+      if (need > act) act = need;
+      nms::ProdDesc pd;
+      memset(&pd, 0, sizeof(pd));
+      for (int k = 0; k < sg.g.nseg; ++k) {
+        pd.w[k] = sg.g.seg[k].w;
+        pd.row_start[k] = sg.g.seg[k].row_start;
+      }
+      pd.rows_total = sg.g.rows_total;
+      pd.row_groups = sg.g.row_groups;
+      pd.w_pad = sg.g.w_pad;
+      pd.nseg = (int16_t)sg.g.nseg;
+      pd.paired = paired ? 1 : 0;
+      pd.lanes = (int8_t)sg.lanes;
+      kinds.push_back(nms::kStageGemv);
+      gemvs.push_back(sg);
+      descs.push_back(pd);
     } else if (r.kind == LaunchRec::kAttention) {
       if (r.ap.splits > nms::kMaxSplits)
         return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: %d attention splits (max %d)", i, r.ap.splits, nms::kMaxSplits);
-      st.kind = nms::kStageAttn;
-      st.a = r.ap;
-      st.units = st.a.Hkv * st.a.splits;
-      if (st.units > max_units) max_units = st.units;
-      if (st.a.Hkv > max_hkv) max_hkv = st.a.Hkv;
+      const int units = r.ap.Hkv * r.ap.splits;
+      if (pos_ptr == nullptr) pos_ptr = r.ap.pos;
+      if (r.ap.pos != pos_ptr) return fail(NMS_ERR_VALUE, "record %d: attention stages must share one position", i);
+      if (units > max_units) max_units = units;
+      if (r.ap.Hkv > max_hkv) max_hkv = r.ap.Hkv;
+      kinds.push_back(nms::kStageAttn);
+      attns.push_back(r.ap);
     } else {
       return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: only GEMV and attention launches run in a persistent step", i);
     }
-    stages.push_back(st);
   }
-  if (smem > dev->step_smem_max)
-    return fail(NMS_ERR_NOT_IMPLEMENTED, "persistent step needs %zu bytes of shared memory (limit %zu)", smem,
-                dev->step_smem_max);
-  const size_t stage_bytes = stages.size() * sizeof(nms::StepStage);
-  const size_t bar_off = nms::align_up_sz(stage_bytes, 256);
+  // Shared memory: [rings: 32 warps x D items][working set][stream descriptors][stage kinds].
+  act = nms::align_up_sz(act, 128);
+  const size_t tail_bytes = descs.size() * sizeof(nms::ProdDesc) + nms::align_up_sz(kinds.size() * 4, 16);
+  const size_t ring_unit = (size_t)nms::kStepWarps * nms::kRingItemBytes;
+  int depth = 0;
+  for (int d : {nms::kStepDepthHi, nms::kStepDepthLo})
+    if (depth == 0 && (size_t)d * ring_unit + act + tail_bytes <= dev->step_smem_max) depth = d;
+  if (depth == 0)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "persistent step: a %zu-byte working set leaves no room for the weight rings",
+                act);
+  const size_t ring_bytes = (size_t)depth * ring_unit;
+  const size_t smem = ring_bytes + act + tail_bytes;
+
+  const size_t kind_off = 0;
+  const size_t gemv_off = nms::align_up_sz(kind_off + kinds.size() * 4, 256);
+  const size_t desc_off = nms::align_up_sz(gemv_off + gemvs.size() * sizeof(nms::StepGemv), 256);
+  const size_t attn_off = nms::align_up_sz(desc_off + descs.size() * sizeof(nms::ProdDesc), 256);
+  const size_t bar_off = nms::align_up_sz(attn_off + attns.size() * sizeof(nms::AttnParams), 256);
   const size_t part_off = bar_off + 256;
   const size_t part_bytes = (size_t)max_units * nms::kAttnMaxGroup * (nms::kAttnD + 2) * sizeof(float);
   const size_t cnt_off = nms::align_up_sz(part_off + part_bytes, 256);
@@ -800,31 +842,49 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
   cudaError_t e = cudaGetDevice(&st->device);
   if (e == cudaSuccess) e = cudaMalloc(&st->dev_mem, total);
   if (e == cudaSuccess) e = cudaMemset(st->dev_mem, 0, total);
-  if (e == cudaSuccess) e = cudaMemcpy(st->dev_mem, stages.data(), stage_bytes, cudaMemcpyHostToDevice);
+  unsigned char* base = static_cast<unsigned char*>(st->dev_mem);
+  if (e == cudaSuccess) e = cudaMemcpy(base + kind_off, kinds.data(), kinds.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && !gemvs.empty())
+    e = cudaMemcpy(base + gemv_off, gemvs.data(), gemvs.size() * sizeof(nms::StepGemv), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && !descs.empty())
+    e = cudaMemcpy(base + desc_off, descs.data(), descs.size() * sizeof(nms::ProdDesc), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && !attns.empty())
+    e = cudaMemcpy(base + attn_off, attns.data(), attns.size() * sizeof(nms::AttnParams), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     if (st->dev_mem) cudaFree(st->dev_mem);
     delete st;
     return fail_cuda(e, "persistent step set-up");
   }
-  unsigned char* base = static_cast<unsigned char*>(st->dev_mem);
-  st->nstages = (int)stages.size();
+  st->nstages = (int)kinds.size();
   st->grid = grid;
   st->smem = smem;
-  st->params.stages = reinterpret_cast<const nms::StepStage*>(base);
-  st->params.nstages = st->nstages;
-  st->params.bar_count = reinterpret_cast<unsigned*>(base + bar_off);
-  st->params.bar_exit = reinterpret_cast<unsigned*>(base + bar_off + 128);
-  st->params.attn_part = reinterpret_cast<float*>(base + part_off);
-  st->params.attn_count = reinterpret_cast<unsigned*>(base + cnt_off);
-  st->params.trace = nullptr;
+  st->depth = depth;
+  nms::StepParams& P = st->params;
+  P.kind = reinterpret_cast<const int32_t*>(base + kind_off);
+  P.gemv = reinterpret_cast<const nms::StepGemv*>(base + gemv_off);
+  P.desc = reinterpret_cast<const nms::ProdDesc*>(base + desc_off);
+  P.attn = reinterpret_cast<const nms::AttnParams*>(base + attn_off);
+  P.nstages = st->nstages;
+  P.ngemv = (int32_t)gemvs.size();
+  P.nattn = (int32_t)attns.size();
+  P.ring_bytes = (int32_t)ring_bytes;
+  P.act_bytes = (int32_t)act;
+  P.bar_count = reinterpret_cast<unsigned*>(base + bar_off);
+  P.bar_exit = reinterpret_cast<unsigned*>(base + bar_off + 128);
+  P.attn_part = reinterpret_cast<float*>(base + part_off);
+  P.attn_count = reinterpret_cast<unsigned*>(base + cnt_off);
+  P.trace = nullptr;
+  P.pos = pos_ptr;
   *out = st;
   return NMS_OK;
 }
 
 int nms_step_launch(const nms_step* step, void* stream) {
   if (step == nullptr) return fail(NMS_ERR_VALUE, "step is null");
-  cudaError_t e = launch_ex2(nms::decode_step_kernel, dim3(step->grid), dim3(nms::kStepThreads), step->smem,
-                             static_cast<cudaStream_t>(stream), false, dim3(1, 1, 1), true, step->params);
+  cudaError_t e = launch_ex2(step->depth == nms::kStepDepthHi ? nms::decode_step_kernel<nms::kStepDepthHi>
+                                                             : nms::decode_step_kernel<nms::kStepDepthLo>,
+                             dim3(step->grid), dim3(nms::kStepThreads), step->smem, static_cast<cudaStream_t>(stream),
+                             false, dim3(1, 1, 1), true, step->params);
   if (e != cudaSuccess) return fail_cuda(e, "decode_step_kernel launch");
   return NMS_OK;
 }

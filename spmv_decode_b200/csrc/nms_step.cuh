@@ -1,23 +1,24 @@
 // Persistent decode step: every stage of one decode step (per layer: q/k/v
 // GEMV, attention, o-projection, gate/up + SwiGLU, down-projection; then the
 // output head with greedy argmax) runs inside ONE cooperative launch of one
-// 1024-thread CTA per SM.
+// 512-thread CTA per SM (16 warps with up to 128 registers each: the
+// streaming loop, its copy producer and the stage prologues fit without
+// spilling).
 //
 // Why: a batch-1 decode step is ~160 small HBM-bound launches.  Each launch
 // pays a fixed cost (CTA start-up, the first loads' latency, the prologue,
 // the tail) of several microseconds during which HBM idles.  Inside one
 // persistent kernel the stages are separated by grid barriers instead, and
-// before a CTA waits at a barrier it already issues the next GEMV stage's
-// first weight loads (weights never depend on activations) and stages that
-// stage's mask offsets, so the memory system keeps streaming through the
-// barrier.
+// every warp streams its weights through a shared-memory ring whose copies
+// run ahead of the computation across stage boundaries (weights never
+// depend on activations), so HBM keeps streaming while a CTA waits at a
+// barrier, normalises its input or runs attention.
 //
-// Grid barrier: arrival counter + generation word in global memory (reset
-// by the last arriver, generation monotonic across launches); waits are
-// bounded by %globaltimer and record kDevBarrierTimeout instead of hanging.
-// Attention: one (KV head, context split) unit per CTA; the last unit of a
-// head to finish (per-head arrival counter) combines the splits' partial
-// softmax states from L2.
+// Grid barrier: a monotonic arrival counter in global memory (reset by the
+// last CTA to leave); waits are bounded by %globaltimer and record
+// kDevBarrierTimeout instead of hanging.  Attention: one (KV head, context
+// split) unit per CTA; the last unit of a head to finish (per-head arrival
+// counter) combines the splits' partial softmax states from L2.
 #pragma once
 
 #include "nms_common.cuh"
@@ -26,26 +27,27 @@
 
 namespace nms {
 
-constexpr int kStepThreads = 1024;
+#ifndef NMS_STEP_THREADS
+#define NMS_STEP_THREADS 512
+#endif
+constexpr int kStepThreads = NMS_STEP_THREADS;
 constexpr int kStepWarps = kStepThreads / kWarp;
-constexpr int kStepU = 4;  // register ring depth (32-byte loads per lane)
 constexpr uint64_t kBarrierLimitNs = 200ull * 1000 * 1000;
 constexpr int kMaxSplits = 16;  // attention splits per KV head (cluster-size bound of the standalone kernel)
 
 enum StageKind : int32_t { kStageGemv = 0, kStageAttn = 1 };
 
-struct StepStage {
-  int32_t kind;
-  int32_t units;  // attention: KV heads x splits
-  int32_t lanes;  // GEMV: lanes per packed row (32, 16, 8 or 4)
-  int32_t pad_;
-  GemvParams g;
-  AttnParams a;
-};
+struct StepGemv;
+struct ProdDesc;
 
 struct StepParams {
-  const StepStage* stages;  // device array
-  int32_t nstages;
+  const int32_t* kind;      // [nstages] StageKind
+  const StepGemv* gemv;     // [ngemv] GEMV stages in step order
+  const ProdDesc* desc;     // [ngemv] their weight-stream descriptors
+  const AttnParams* attn;   // [nattn] attention stages in step order
+  int32_t nstages, ngemv, nattn;
+  int32_t ring_bytes;       // kStepWarps * D * kRingItemBytes, at the start of dynamic shared memory
+  int32_t act_bytes;        // working set after the rings (GEMV or attention); then desc[ngemv], kind[nstages]
   unsigned* bar_count;      // grid barrier arrivals (grows within a launch, reset at exit)
   unsigned* bar_exit;       // CTAs that have left the kernel (reset at exit)
   float* attn_part;         // [units][kAttnMaxGroup][kAttnD + 2] partial softmax states
@@ -54,6 +56,7 @@ struct StepParams {
   // trace[1 + s*(ncta+1) + c] = time CTA c finished stage s's work;
   // trace[1 + s*(ncta+1) + ncta] = time CTA 0 left the barrier after stage s.
   unsigned long long* trace;
+  const int64_t* pos;       // token position of the step (all attention stages)
 };
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -123,140 +126,269 @@ __device__ __forceinline__ void cp_async_commit_wait_all() {
 }
 
 // ---------------------------------------------------------------------------
-// GEMV stage, split in the part that may run before the barrier (weights and
-// masks only) and the part after it.
+// Weight streams.  Each warp owns a contiguous range of work items of every
+// GEMV stage (an item: RG = 32/L rows x 16L halves, 32 bytes per lane) and
+// streams them through its own shared-memory ring of D items with 16-byte
+// cp.async copies (two per lane and item).  The producer side of the ring
+// walks the warp's items of every GEMV stage of the step in order (a compact
+// descriptor of every stage stays in shared memory), so the copies for the
+// next stage are in flight while the CTA runs its epilogue, waits at the grid
+// barrier, normalises the next input or runs attention -- weights never
+// depend on activations.  Every consumed item commits exactly one copy group
+// (empty past the step's last item), so `cp.async.wait_group D-1` always
+// waits for exactly the item about to be read.  A lane only reads back the
+// 32 bytes it copied itself.  Every active warp gets at least one row of
+// items, so a row is split over at most two warps and its two shared-memory
+// partial sums add in either order to the same value: results are
+// deterministic.
 // ---------------------------------------------------------------------------
-struct StepGemvSmem {
-  __half* xs;
-  uint8_t* sidx;
-  __half* xc;
-  float* acc;
-  float* red;
+constexpr int kRingItemBytes = kWarp * 32;
+constexpr uint64_t kPreWaitLimitNs = 200ull * 1000 * 1000;
+
+struct StepGemv {
+  GemvParams g;
+  int32_t lanes;  // L: lanes per row (32, 16, 8 or 4), w_pad % (16 L) == 0
+  int32_t pad_[3];
 };
 
-__device__ __forceinline__ StepGemvSmem step_gemv_smem(const GemvParams& p, unsigned char* base, int max_vrows,
-                                                       int nsegx) {
-  StepGemvSmem s;
-  size_t off = 0;
-  s.xs = reinterpret_cast<__half*>(base + off);
-  off += align_up_sz((size_t)p.K * 2, 16);
-  s.sidx = base + off;
-  off += align_up_sz((size_t)p.w, 16) * nsegx;
-  s.xc = reinterpret_cast<__half*>(base + off);
-  off += align_up_sz((size_t)p.w_pad * 2 * nsegx, 16);
-  s.acc = reinterpret_cast<float*>(base + off);
-  off += align_up_sz((size_t)max_vrows * 4, 16);
-  s.red = reinterpret_cast<float*>(base + off);
-  return s;
+// What the producer needs of a GEMV stage (64 bytes, all stages resident).
+struct ProdDesc {
+  const __half* w[kMaxSegs];
+  int32_t row_start[kMaxSegs];
+  int32_t rows_total, row_groups, w_pad;
+  int16_t nseg;
+  int8_t paired;
+  int8_t lanes;
+};
+static_assert(sizeof(ProdDesc) == 64, "ProdDesc is 64 bytes");
+
+__host__ __device__ inline int ring_lanes(int w_pad) {
+  return (w_pad % 512 == 0) ? 32 : (w_pad % 256 == 0) ? 16 : (w_pad % 128 == 0) ? 8 : 4;
 }
 
-struct GemvGeom {
-  int g0, ng, vgroups, cpr, t0, t1, max_vrows, nsegx;
-  bool paired, dense;
+// A CTA's row groups [g0, g0 + ng) and a warp's items [t0, t1) of a stage.
+struct WarpGeom {
+  int cpr, g0, ng, t0, t1;
 };
 
-template <int L>
-__device__ __forceinline__ GemvGeom gemv_geom(const GemvParams& p, unsigned cta, unsigned ncta) {
-  constexpr int RG = kWarp / L;
-  GemvGeom q;
-  q.paired = (p.mode == kModePaired);
-  q.nsegx = q.paired ? 2 : p.nseg;
-  q.dense = (p.seg[0].idx == nullptr);
-  q.g0 = (int)(((int64_t)cta * p.row_groups) / ncta);
-  const int g1 = (int)(((int64_t)(cta + 1) * p.row_groups) / ncta);
-  q.ng = g1 - q.g0;
-  q.vgroups = q.paired ? 2 * q.ng : q.ng;
-  q.max_vrows = (q.paired ? 2 : 1) * ((p.row_groups + ncta - 1) / ncta) * RG;
-  q.cpr = p.w_pad / (16 * L);
-  const int T = q.vgroups * q.cpr;
-  const int warp = threadIdx.x >> 5;
-  q.t0 = (int)(((int64_t)warp * T) / kStepWarps);
-  q.t1 = (int)(((int64_t)(warp + 1) * T) / kStepWarps);
+__device__ __forceinline__ WarpGeom warp_geom(int row_groups, bool paired, int w_pad, int L, unsigned cta,
+                                              unsigned ncta, int warp) {
+  WarpGeom q;
+  q.cpr = w_pad / (16 * L);
+  q.g0 = (int)(((unsigned)cta * (unsigned)row_groups) / ncta);
+  q.ng = (int)(((unsigned)(cta + 1) * (unsigned)row_groups) / ncta) - q.g0;
+  const int vgroups = paired ? 2 * q.ng : q.ng;
+  const unsigned T = (unsigned)(vgroups * q.cpr);
+  const int nw = max(1, min(kStepWarps, vgroups));  // >= cpr items per active warp
+  if (warp < nw) {
+    q.t0 = (int)(((unsigned)warp * T) / (unsigned)nw);
+    q.t1 = (int)(((unsigned)(warp + 1) * T) / (unsigned)nw);
+  } else {
+    q.t0 = q.t1 = (int)T;
+  }
   return q;
 }
 
-// This CTA's rows of a GEMV stage (every segment) into L2, in bulk prefetches
-// issued by one thread -- used while the grid runs a latency-bound stage.
-template <int L>
-__device__ __forceinline__ void gemv_l2_prefetch_own(const GemvParams& p, const GemvGeom& q) {
-  constexpr int RG = kWarp / L;
-  if (threadIdx.x != 0 || q.ng <= 0) return;
-  const int r0 = q.g0 * RG;
-  const int r1 = min((q.g0 + q.ng) * RG, p.rows_total);
-  for (int sx = 0; sx < p.nseg; ++sx) {
-    int a = r0, b = r1;
-    if (!q.paired) {
-      a = max(r0, p.seg[sx].row_start) - p.seg[sx].row_start;
-      b = min(r1, p.seg[sx].row_start + p.seg[sx].rows) - p.seg[sx].row_start;
-    }
-    if (a >= b) continue;
-    const char* base = reinterpret_cast<const char*>(p.seg[sx].w + (size_t)a * p.w_pad);
-    const size_t bytes = (size_t)(b - a) * p.w_pad * 2;
-    for (size_t o = 0; o < bytes; o += 65536) {
-      const size_t n = bytes - o < 65536 ? bytes - o : 65536;
-      bulk_prefetch_l2(base + o, (uint32_t)n);
-    }
-  }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Pre-barrier: the first kStepU loads of this warp into the register ring and
-// the mask offsets into shared memory (plain 16-byte loads).
-template <int L>
-__device__ __forceinline__ void gemv_pre(const GemvParams& p, const GemvGeom& q, unsigned char* smem_base,
-                                         U32x8 (&buf)[kStepU]) {
-  constexpr int RG = kWarp / L, CH = 16 * L;
-  const int lane = threadIdx.x & 31, sub = lane / L, li = lane % L;
-  int vg = q.t0 / q.cpr, c = q.t0 - vg * q.cpr;
-  LaneRow r = lane_row(p, q.paired, q.g0, q.ng, vg, RG, sub);
+// Producer side of a warp's ring (lane-private registers; every lane runs it).
+struct Prod {
+  int n;          // GEMV ordinal whose items are being issued
+  int t, t1;      // next item, end of this warp's items in that stage
+  int vg, c, cpr; // row group, column item, items per row group
+  int g0, ng;     // the CTA's row groups of the stage
+  int cstep;      // bytes per column item (32 L)
+  int slot;       // next ring slot
+  const unsigned char* src;  // this lane's source at column item c of its row
+  bool valid;
+};
+
+__device__ __forceinline__ void prod_row(Prod& P, const ProdDesc& d) {
+  const int lane = threadIdx.x & 31, L = d.lanes, RG = kWarp / L;
+  const int sub = lane / L, li = lane % L;
+  int grow, segi = 0;
+  if (d.paired) {
+    segi = (P.vg >= P.ng) ? 1 : 0;
+    grow = (P.g0 + P.vg - segi * P.ng) * RG + sub;
+  } else {
+    grow = (P.g0 + P.vg) * RG + sub;
 #pragma unroll
-  for (int u = 0; u < kStepU; ++u) {
-    // Every slot is written (zeros past the range) so the ring carries no
-    // value across stages that do not refill it.
-    if (q.t0 + u < q.t1 && r.valid) {
-      buf[u] = ld_stream_256(p.seg[r.segi].w + (size_t)r.lrow * p.w_pad + li * 16 + (size_t)c * CH);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) buf[u].v[e] = 0u;
-    }
-    if (q.t0 + u < q.t1) {
-      if (++c == q.cpr) {
-        c = 0;
-        ++vg;
-        r = lane_row(p, q.paired, q.g0, q.ng, vg, RG, sub);
-      }
-    }
+    for (int k = 1; k < kMaxSegs; ++k)
+      if (k < d.nseg && grow >= d.row_start[k]) segi = k;
   }
-  if (!q.dense) {
-    StepGemvSmem s = step_gemv_smem(p, smem_base, q.max_vrows, q.nsegx);
-    const int w_al = (int)align_up_sz((size_t)p.w, 16);
-    const bool vec = (p.w & 15) == 0;
-    for (int sx = 0; sx < q.nsegx; ++sx) {
-      const uint8_t* src = p.seg[sx].idx;
-      uint8_t* dst = s.sidx + (size_t)sx * w_al;
-      if (vec && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
-        // Asynchronous copies: nothing here waits for them; gemv_post does.
-        for (int i = threadIdx.x; i < p.w / 16; i += kStepThreads)
-          cp_async_16(reinterpret_cast<uint4*>(dst) + i, reinterpret_cast<const uint4*>(src) + i);
+  P.valid = grow < d.rows_total;
+  const int lrow = P.valid ? grow - (d.paired ? 0 : d.row_start[segi]) : 0;
+  P.src = reinterpret_cast<const unsigned char*>(d.w[segi] + (size_t)lrow * d.w_pad) + li * 16 + P.c * P.cstep;
+}
+
+__device__ __forceinline__ void prod_setup(Prod& P, const ProdDesc& d, int n, unsigned cta, unsigned ncta) {
+  const WarpGeom q = warp_geom(d.row_groups, d.paired != 0, d.w_pad, d.lanes, cta, ncta, threadIdx.x >> 5);
+  P.n = n;
+  P.t = q.t0;
+  P.t1 = q.t1;
+  P.cpr = q.cpr;
+  P.g0 = q.g0;
+  P.ng = q.ng;
+  P.cstep = 32 * d.lanes;
+  P.vg = q.t0 / q.cpr;
+  P.c = q.t0 - P.vg * q.cpr;
+  if (q.t0 < q.t1) prod_row(P, d);
+}
+
+// Commit one copy group: the warp's next item (moving on through the step's
+// GEMV stages as needed), or an empty group past the last one.
+template <int D>
+__device__ __forceinline__ void prod_next(Prod& P, const ProdDesc* descs, int ngemv, unsigned char* wring,
+                                          unsigned cta, unsigned ncta) {
+  while (P.t >= P.t1 && P.n + 1 < ngemv) prod_setup(P, descs[P.n + 1], P.n + 1, cta, ncta);
+  if (P.t < P.t1) {
+    if (P.valid) {
+      // Lane slots: first 16 bytes at +lane*16, second at +512 + lane*16
+      // (conflict-free reads).
+      unsigned char* dst = wring + P.slot * kRingItemBytes + (threadIdx.x & 31) * 16;
+      cp_async_16(dst, P.src);
+      cp_async_16(dst + 512, P.src + P.cstep / 2);
+    }
+    ++P.t;
+    P.src += P.cstep;
+    if (++P.c == P.cpr) {
+      P.c = 0;
+      ++P.vg;
+      if (P.t < P.t1) prod_row(P, descs[P.n]);
+    }
+    P.slot = (P.slot + 1 == D) ? 0 : P.slot + 1;
+  }
+  cp_async_commit();
+}
+
+struct Ring {
+  unsigned char* wring;  // this warp's D item slots
+  int cslot;             // slot of the next item to consume
+  Prod P;
+};
+
+// ---------------------------------------------------------------------------
+// GEMV stage working set in shared memory (after the rings).
+// ---------------------------------------------------------------------------
+struct StepGemvSmem {
+  __half* xs;     // [K] input after the residual add
+  uint8_t* sidx;  // [nsegx][w_al] mask offsets
+  __half* xc;     // [nsegx][w_pad] gathered input (natural order)
+  __half* nw;     // [K] RMSNorm weight (norm prologue only)
+  float* acc;     // [max_vrows] row sums
+  float* red;     // [32] block reduction
+};
+
+__host__ __device__ inline size_t step_gemv_layout(int K, int w, int w_pad, int nsegx, int max_vrows, bool norm,
+                                                   size_t* off_sidx, size_t* off_xc, size_t* off_nw, size_t* off_acc,
+                                                   size_t* off_red) {
+  size_t off = align_up_sz((size_t)K * 2, 16);
+  *off_sidx = off;
+  off += align_up_sz((size_t)w, 16) * nsegx;
+  *off_xc = off;
+  off += align_up_sz((size_t)w_pad * 2 * nsegx, 16);
+  *off_nw = off;
+  if (norm) off += align_up_sz((size_t)K * 2, 16);
+  *off_acc = off;
+  off += align_up_sz((size_t)max_vrows * 4, 16);
+  *off_red = off;
+  off += 32 * 4;
+  return off;
+}
+
+__host__ __device__ inline size_t step_gemv_smem_bytes(int K, int w, int w_pad, int nsegx, int max_vrows, bool norm) {
+  size_t a, b, c, d, e;
+  return step_gemv_layout(K, w, w_pad, nsegx, max_vrows, norm, &a, &b, &c, &d, &e);
+}
+
+__device__ __forceinline__ StepGemvSmem step_gemv_smem(const GemvParams& p, unsigned char* base, int nsegx,
+                                                       int max_vrows) {
+  size_t o_sidx, o_xc, o_nw, o_acc, o_red;
+  step_gemv_layout(p.K, p.w, p.w_pad, nsegx, max_vrows, p.prologue == kProResidNorm, &o_sidx, &o_xc, &o_nw, &o_acc,
+                   &o_red);
+  StepGemvSmem s;
+  s.xs = reinterpret_cast<__half*>(base);
+  s.sidx = base + o_sidx;
+  s.xc = reinterpret_cast<__half*>(base + o_xc);
+  s.nw = reinterpret_cast<__half*>(base + o_nw);
+  s.acc = reinterpret_cast<float*>(base + o_acc);
+  s.red = reinterpret_cast<float*>(base + o_red);
+  return s;
+}
+
+__device__ __forceinline__ int stage_nsegx(const GemvParams& p) { return p.mode == kModePaired ? 2 : p.nseg; }
+__device__ __forceinline__ int stage_max_vrows(const GemvParams& p, int RG, unsigned ncta) {
+  return (p.mode == kModePaired ? 2 : 1) * ((p.row_groups + (int)ncta - 1) / (int)ncta) * RG;
+}
+
+// Mask offsets and RMSNorm weights of a GEMV stage: staged into the working
+// set while the CTA waits at the grid barrier before the stage, by bulk
+// copies (one thread issues; completion on an mbarrier, one phase per stage
+// that uses it) when every piece is 16-byte shaped, else by plain loads.
+__device__ __forceinline__ bool pre_bulk(const GemvParams& p) {
+  if (p.seg[0].idx != nullptr) {
+    if ((p.w & 15) != 0) return false;
+    for (int sx = 0; sx < stage_nsegx(p); ++sx)
+      if ((reinterpret_cast<uintptr_t>(p.seg[sx].idx) & 15u) != 0) return false;
+  }
+  if (p.prologue == kProResidNorm && ((p.K & 7) != 0 || (reinterpret_cast<uintptr_t>(p.norm_w) & 15u) != 0))
+    return false;
+  return true;
+}
+
+__device__ __forceinline__ void gemv_pre_smem(const StepGemv& sg, unsigned ncta, unsigned char* act, uint64_t* bar,
+                                              unsigned& uses) {
+  const GemvParams& p = sg.g;
+  const int nsegx = stage_nsegx(p);
+  StepGemvSmem s = step_gemv_smem(p, act, nsegx, stage_max_vrows(p, kWarp / sg.lanes, ncta));
+  const int w_al = (int)align_up_sz((size_t)p.w, 16);
+  const bool has_idx = p.seg[0].idx != nullptr, norm = p.prologue == kProResidNorm;
+  if (pre_bulk(p)) {
+    if (threadIdx.x == 0) {
+      const uint32_t bytes = (has_idx ? (uint32_t)(nsegx * p.w) : 0u) + (norm ? (uint32_t)p.K * 2u : 0u);
+      if (bytes > 0) {
+        fence_proxy_async_smem();  // the CTA's earlier use of this memory (ordered by the block barrier) first
+        mbar_arrive_expect_tx(bar, bytes);
+        if (has_idx)
+          for (int sx = 0; sx < nsegx; ++sx) bulk_copy_g2s(s.sidx + (size_t)sx * w_al, p.seg[sx].idx, p.w, bar);
+        if (norm) bulk_copy_g2s(s.nw, p.norm_w, (uint32_t)p.K * 2u, bar);
       } else {
-        for (int i = threadIdx.x; i < p.w; i += kStepThreads) dst[i] = src[i];
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
       }
     }
+    ++uses;
+    return;
   }
+  if (has_idx)
+    for (int sx = 0; sx < nsegx; ++sx)
+      for (int i = threadIdx.x; i < p.w; i += kStepThreads) s.sidx[(size_t)sx * w_al + i] = p.seg[sx].idx[i];
+  if (norm)
+    for (int i = threadIdx.x; i < p.K; i += kStepThreads) s.nw[i] = p.norm_w[i];
 }
 
-// Post-barrier: input prologue, gather, streaming, epilogue.
-template <int L>
-__device__ __forceinline__ void gemv_post(const GemvParams& p, const GemvGeom& q, unsigned char* smem_base,
-                                          U32x8 (&buf)[kStepU], unsigned cta, unsigned ncta) {
-  constexpr int RG = kWarp / L, CH = 16 * L, U = kStepU, NT = kStepThreads;
+// One GEMV stage after its barrier: input prologue (residual add, RMSNorm
+// statistic), gather, this warp's items from its ring (each consumed item
+// commits the warp's next copy), epilogue.
+template <int L, int D>
+__device__ __forceinline__ void gemv_stage(const StepGemv& sg, const ProdDesc* descs, int ngemv, unsigned cta,
+                                           unsigned ncta, unsigned char* act, Ring& R, uint64_t* pre_bar,
+                                           unsigned pre_uses) {
+  constexpr int RG = kWarp / L, NT = kStepThreads, CB = 32 * L;
+  const GemvParams& p = sg.g;
   const int tid = threadIdx.x, lane = tid & 31;
   const int sub = lane / L, li = lane % L;
-  StepGemvSmem s = step_gemv_smem(p, smem_base, q.max_vrows, q.nsegx);
+  const WarpGeom q = warp_geom(p.row_groups, p.mode == kModePaired, p.w_pad, L, cta, ncta, tid >> 5);
+  const bool paired = (p.mode == kModePaired);
+  const int nsegx = stage_nsegx(p);
+  const bool dense = (p.seg[0].idx == nullptr);
+  const int max_vrows = stage_max_vrows(p, RG, ncta);
+  StepGemvSmem s = step_gemv_smem(p, act, nsegx, max_vrows);
   const int w_al = (int)align_up_sz((size_t)p.w, 16);
 
-  // Mask offsets staged by gemv_pre's asynchronous copies (no-op if none).
-  cp_async_commit_wait_all();
-  // Input vector (+ residual) into shared memory, with the RMSNorm statistic.
   const __half* xsrc = input_row(p);
   const bool resid = (p.prologue == kProResidNorm);
   const bool add = resid && (p.x2 != nullptr);
@@ -287,7 +419,7 @@ __device__ __forceinline__ void gemv_post(const GemvParams& p, const GemvGeom& q
       ss = fmaf(v, v, ss);
     }
   }
-  for (int v = tid; v < q.vgroups * RG; v += NT) s.acc[v] = 0.f;
+  for (int v = tid; v < max_vrows; v += NT) s.acc[v] = 0.f;
   float rstd = 1.f;
   if (resid) {
     const float tot = block_reduce_sum(ss, s.red);
@@ -296,84 +428,59 @@ __device__ __forceinline__ void gemv_post(const GemvParams& p, const GemvGeom& q
   __syncthreads();
   if (resid && p.resid_out != nullptr && cta == 0)
     for (int i = tid; i < p.K; i += NT) p.resid_out[i] = s.xs[i];
-
-  // Gather the compressed vectors (permuted for conflict-free reads).
-  for (int sx = 0; sx < q.nsegx; ++sx) {
+  if (pre_bulk(p)) mbar_wait_bounded(pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);  // staged masks / norm
+  // Gather (consecutive threads take consecutive kept positions: their mask
+  // group and so their shared-memory reads stay together).
+  const int n_shift = ((p.n & (p.n - 1)) == 0) ? __ffs(p.n) - 1 : -1;
+  for (int sx = 0; sx < nsegx; ++sx) {
     const uint8_t* idx = s.sidx + (size_t)sx * w_al;
     __half* xc = s.xc + (size_t)sx * p.w_pad;
     for (int j = tid; j < p.w_pad; j += NT) {
       __half val = __ushort_as_half((unsigned short)0);
       if (j < p.w) {
-        const int col = q.dense ? j : (j / p.n) * p.m + (int)idx[j];
+        const int grp = n_shift >= 0 ? (j >> n_shift) : j / p.n;
+        const int col = dense ? j : grp * p.m + (int)idx[j];
         if (col < p.K) {
           val = s.xs[col];
-          if (resid) val = f2h(h2f(f2h(h2f(val) * rstd)) * h2f(p.norm_w[col]));
+          if (resid) val = f2h(h2f(f2h(h2f(val) * rstd)) * h2f(s.nw[col]));
         }
       }
-      xc[xc_perm<L>(j)] = val;
+      xc[j] = val;
     }
   }
   __syncthreads();
 
-  // Stream: the ring holds items t0 .. t0+U-1; the load cursor starts at t0+U.
-  int l_vg, l_c;
-  {
-    const int ls = min(q.t1, q.t0 + U);
-    l_vg = ls / q.cpr;
-    l_c = ls - l_vg * q.cpr;
-  }
-  LaneRow lr = lane_row(p, q.paired, q.g0, q.ng, l_vg, RG, sub);
-  const __half* l_ptr = p.seg[lr.segi].w + (size_t)lr.lrow * p.w_pad + li * 16;
-  bool l_valid = lr.valid;
-  int c_vg = q.t0 / q.cpr, c_c = q.t0 - c_vg * q.cpr;
-  LaneRow cr = lane_row(p, q.paired, q.g0, q.ng, c_vg, RG, sub);
-  bool c_valid = cr.valid;
-  const __half* xcs = s.xc + (size_t)cr.segi * p.w_pad + li * 8;
-  float a0 = 0.f, a1 = 0.f;
-  for (int base = q.t0; base < q.t1; base += U) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = base + u;
-      if (t < q.t1) {
-        const uint4 xa = *reinterpret_cast<const uint4*>(xcs + c_c * CH);
-        const uint4 xb = *reinterpret_cast<const uint4*>(xcs + c_c * CH + 8 * L);
-        fma2_f32_f16(a0, a1, buf[u].v[0], xa.x);
-        fma2_f32_f16(a0, a1, buf[u].v[1], xa.y);
-        fma2_f32_f16(a0, a1, buf[u].v[2], xa.z);
-        fma2_f32_f16(a0, a1, buf[u].v[3], xa.w);
-        fma2_f32_f16(a0, a1, buf[u].v[4], xb.x);
-        fma2_f32_f16(a0, a1, buf[u].v[5], xb.y);
-        fma2_f32_f16(a0, a1, buf[u].v[6], xb.z);
-        fma2_f32_f16(a0, a1, buf[u].v[7], xb.w);
-        if (t + U < q.t1) {
-          if (l_valid) {
-            buf[u] = ld_stream_256(l_ptr + (size_t)l_c * CH);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) buf[u].v[e] = 0u;
-          }
-          if (++l_c == q.cpr) {
-            l_c = 0;
-            ++l_vg;
-            lr = lane_row(p, q.paired, q.g0, q.ng, l_vg, RG, sub);
-            l_valid = lr.valid;
-            l_ptr = p.seg[lr.segi].w + (size_t)lr.lrow * p.w_pad + li * 16;
-          }
-        }
-        const bool row_end = (++c_c == q.cpr);
-        if (row_end || t + 1 == q.t1) {
-          const float tot = group_reduce_sum<L>(a0 + a1);
-          if (li == 0 && c_valid) atomicAdd(&s.acc[c_vg * RG + sub], tot);
-          a0 = a1 = 0.f;
-          if (row_end) {
-            c_c = 0;
-            ++c_vg;
-            if (c_vg < q.vgroups) {
-              cr = lane_row(p, q.paired, q.g0, q.ng, c_vg, RG, sub);
-              c_valid = cr.valid;
-              xcs = s.xc + (size_t)cr.segi * p.w_pad + li * 8;
-            }
-          }
+  if (q.t0 < q.t1) {
+    int vg = q.t0 / q.cpr, c = q.t0 - vg * q.cpr;
+    LaneRow r = lane_row(p, paired, q.g0, q.ng, vg, RG, sub);
+    const unsigned char* xcs = reinterpret_cast<const unsigned char*>(s.xc + (size_t)r.segi * p.w_pad) + li * 16;
+    float a0 = 0.f, a1 = 0.f;
+    for (int t = q.t0; t < q.t1; ++t) {
+      cp_async_wait<D - 1>();
+      const unsigned char* slot = R.wring + R.cslot * kRingItemBytes + lane * 16;
+      const uint4 wa = *reinterpret_cast<const uint4*>(slot);
+      const uint4 wb = *reinterpret_cast<const uint4*>(slot + 512);
+      const uint4 xa = *reinterpret_cast<const uint4*>(xcs + c * CB);
+      const uint4 xb = *reinterpret_cast<const uint4*>(xcs + c * CB + CB / 2);
+      fma2_f32_f16(a0, a1, wa.x, xa.x);
+      fma2_f32_f16(a0, a1, wa.y, xa.y);
+      fma2_f32_f16(a0, a1, wa.z, xa.z);
+      fma2_f32_f16(a0, a1, wa.w, xa.w);
+      fma2_f32_f16(a0, a1, wb.x, xb.x);
+      fma2_f32_f16(a0, a1, wb.y, xb.y);
+      fma2_f32_f16(a0, a1, wb.z, xb.z);
+      fma2_f32_f16(a0, a1, wb.w, xb.w);
+      R.cslot = (R.cslot + 1 == D) ? 0 : R.cslot + 1;
+      prod_next<D>(R.P, descs, ngemv, R.wring, cta, ncta);
+      if (++c == q.cpr || t + 1 == q.t1) {
+        const float tot = group_reduce_sum<L>(a0 + a1);
+        if (li == 0 && r.valid) atomicAdd(&s.acc[vg * RG + sub], tot);
+        a0 = a1 = 0.f;
+        if (c == q.cpr && t + 1 < q.t1) {
+          c = 0;
+          ++vg;
+          r = lane_row(p, paired, q.g0, q.ng, vg, RG, sub);
+          xcs = reinterpret_cast<const unsigned char*>(s.xc + (size_t)r.segi * p.w_pad) + li * 16;
         }
       }
     }
@@ -399,17 +506,16 @@ struct StepAttnSmem {
   int last;
 };
 
-__device__ __forceinline__ void attention_unit(const AttnParams& p, int split, int kvh, StepAttnSmem& S,
+__device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, int split, int kvh, StepAttnSmem& S,
                                                float* part, unsigned* head_count) {
   constexpr int D = kAttnD, PT = kAttnTile, GM = kAttnMaxGroup, NT = kStepThreads;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = p.Hq / p.Hkv;
-  const int64_t pos64 = *p.pos;
-  if (pos64 < 0 || pos64 >= p.S_max) {  // uniform: every CTA reads the same value
+  if (pos_in < 0 || pos_in >= p.S_max) {  // uniform: every CTA read the same value
     if (tid == 0 && split == 0 && kvh == 0) set_device_error(kDevBadPosition);
     return;
   }
-  const int pos = (int)pos64;
+  const int pos = pos_in;
   const int P = pos + 1;
   const int pb = (int)(((int64_t)split * P) / p.splits);
   const int pe = (int)(((int64_t)(split + 1) * P) / p.splits);
@@ -417,27 +523,46 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int split, i
   const __half* rope_row = p.rope + (size_t)pos * D;
   const __half* kbase = p.k_cache + (size_t)kvh * p.S_max * D;
   const __half* vbase = p.v_cache + (size_t)kvh * p.S_max * D;
-  // K and V rows of a tile: cached rows by asynchronous copies, rows past the
-  // range zero; the new token's row is filled from shared memory later.
-  auto issue_tile = [&](int t0) {
+  // K and V rows of a tile: cached rows by plain 16-byte loads into
+  // registers (kept apart from the weight streams' copy groups), stored to
+  // shared memory once the q / k / v work is done; rows past the range are
+  // zero; the new token's row is filled from shared memory later.  Rows
+  // before `pos` are never written during the step, so they are read through
+  // the non-coherent path.
+  constexpr int PIECES = 2 * PT * (D / 8);
+  constexpr int PPT = (PIECES + NT - 1) / NT;  // pieces per thread
+  uint4 kv[PPT];
+  auto load_tile = [&](int t0) {
     const int nt = min(PT, pe - t0);
-    constexpr int PIECES = 2 * PT * (D / 8);
 #pragma unroll
-    for (int c0 = 0; c0 < PIECES; c0 += NT) {
-      const int c = c0 + tid;
-      if (c >= PIECES) break;
-      const int which = c / (PT * (D / 8));
-      const int rem = c - which * PT * (D / 8);
-      const int r = rem / (D / 8), q8 = rem % (D / 8);
-      __half* dst = which ? &S.sv[r][q8 * 8] : &S.sk[r][q8 * 8];
-      const int tpos = t0 + r;
-      if (r < nt && tpos != pos)
-        cp_async_16(dst, (which ? vbase : kbase) + (size_t)tpos * D + q8 * 8);
-      else if (r >= nt)
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    for (int k = 0; k < PPT; ++k) {
+      const int c = k * NT + tid;
+      kv[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (c < PIECES) {
+        const int which = c / (PT * (D / 8));
+        const int rem = c - which * PT * (D / 8);
+        const int r = rem / (D / 8), q8 = rem % (D / 8);
+        const int tpos = t0 + r;
+        if (r < nt && tpos != pos)
+          kv[k] = __ldg(reinterpret_cast<const uint4*>((which ? vbase : kbase) + (size_t)tpos * D + q8 * 8));
+      }
     }
   };
-  if (pb < pe) issue_tile(pb);  // in flight during the q / k / v work below
+  auto store_tile = [&](int t0) {
+    const int nt = min(PT, pe - t0);
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int c = k * NT + tid;
+      if (c < PIECES) {
+        const int which = c / (PT * (D / 8));
+        const int rem = c - which * PT * (D / 8);
+        const int r = rem / (D / 8), q8 = rem % (D / 8);
+        if (r >= nt || t0 + r != pos)
+          *reinterpret_cast<uint4*>(which ? &S.sv[r][q8 * 8] : &S.sk[r][q8 * 8]) = kv[k];
+      }
+    }
+  };
+  if (pb < pe) load_tile(pb);  // in flight during the q / k / v work below
 
   if (warp < G) {
     const __half* qsrc = p.qkv + (size_t)(kvh * G + warp) * D;
@@ -481,7 +606,8 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int split, i
 
   for (int t0 = pb; t0 < pe; t0 += PT) {
     const int nt = min(PT, pe - t0);
-    if (t0 != pb) issue_tile(t0);
+    if (t0 != pb) load_tile(t0);
+    store_tile(t0);
     __syncthreads();  // knew / vnew (written above) visible
     if (pos >= t0 && pos < t0 + nt) {
       const int r = pos - t0;
@@ -491,7 +617,6 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int split, i
             *reinterpret_cast<const uint4*>((which ? S.vnew : S.knew) + q8 * 8);
       }
     }
-    cp_async_commit_wait_all();
     __syncthreads();
     for (int i = tid; i < G * PT; i += NT) {
       const int g = i / PT, r = i % PT;
@@ -605,88 +730,137 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int split, i
   }
 }
 
+// L2 prefetch of the cached K / V rows this CTA's attention units will read
+// (issued a stage ahead, while HBM streams weights; one thread).
+__device__ __forceinline__ void attn_prefetch_l2(const AttnParams& a, int pos, unsigned cta, unsigned ncta) {
+  if (threadIdx.x != 0 || pos < 0 || pos >= a.S_max) return;
+  const int units = a.Hkv * a.splits, P = pos + 1;
+  for (int u = (int)cta; u < units; u += (int)ncta) {
+    const int split = u % a.splits, kvh = u / a.splits;
+    const int pb = (int)(((int64_t)split * P) / a.splits);
+    const int pe = min((int)(((int64_t)(split + 1) * P) / a.splits), pos);  // row `pos` is written this step
+    if (pe <= pb) continue;
+    const size_t off = ((size_t)kvh * a.S_max + pb) * kAttnD;
+    const uint32_t bytes = (uint32_t)(pe - pb) * kAttnD * 2u;
+    bulk_prefetch_l2(a.k_cache + off, bytes);
+    bulk_prefetch_l2(a.v_cache + off, bytes);
+  }
+}
+
 // ---------------------------------------------------------------------------
-// The persistent kernel.  The lanes-per-row variant of each GEMV stage is
-// chosen per stage, so stages of different packed widths share one launch.
+// The persistent kernel (D: ring depth in items per warp).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void step_gemv_pre(const StepStage& st, unsigned cta, unsigned ncta, unsigned char* smem,
-                                              U32x8 (&buf)[kStepU]) {
-  switch (st.lanes) {
-    case 32: gemv_pre<32>(st.g, gemv_geom<32>(st.g, cta, ncta), smem, buf); break;
-    case 16: gemv_pre<16>(st.g, gemv_geom<16>(st.g, cta, ncta), smem, buf); break;
-    case 8: gemv_pre<8>(st.g, gemv_geom<8>(st.g, cta, ncta), smem, buf); break;
-    default: gemv_pre<4>(st.g, gemv_geom<4>(st.g, cta, ncta), smem, buf); break;
+constexpr int kGemvWords = (int)(sizeof(StepGemv) / 4);
+constexpr int kAttnWords = (int)(sizeof(AttnParams) / 4);
+static_assert(sizeof(StepGemv) % 4 == 0 && sizeof(AttnParams) % 4 == 0, "parameter blocks are copied as words");
+static_assert(kGemvWords <= kStepThreads && kAttnWords <= kStepThreads, "one parameter word per thread");
+
+template <int D>
+__device__ __forceinline__ void run_gemv(const StepGemv& sg, const ProdDesc* descs, int ngemv, unsigned cta,
+                                         unsigned ncta, unsigned char* act, Ring& R, uint64_t* pre_bar,
+                                         unsigned pre_uses) {
+  switch (sg.lanes) {
+    case 32: gemv_stage<32, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
+    case 16: gemv_stage<16, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
+    case 8: gemv_stage<8, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
+    default: gemv_stage<4, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
   }
 }
 
-__device__ __forceinline__ void step_gemv_l2_prefetch(const StepStage& st, unsigned cta, unsigned ncta) {
-  switch (st.lanes) {
-    case 32: gemv_l2_prefetch_own<32>(st.g, gemv_geom<32>(st.g, cta, ncta)); break;
-    case 16: gemv_l2_prefetch_own<16>(st.g, gemv_geom<16>(st.g, cta, ncta)); break;
-    case 8: gemv_l2_prefetch_own<8>(st.g, gemv_geom<8>(st.g, cta, ncta)); break;
-    default: gemv_l2_prefetch_own<4>(st.g, gemv_geom<4>(st.g, cta, ncta)); break;
-  }
-}
-
-__device__ __forceinline__ void step_gemv_post(const StepStage& st, unsigned cta, unsigned ncta, unsigned char* smem,
-                                               U32x8 (&buf)[kStepU]) {
-  switch (st.lanes) {
-    case 32: gemv_post<32>(st.g, gemv_geom<32>(st.g, cta, ncta), smem, buf, cta, ncta); break;
-    case 16: gemv_post<16>(st.g, gemv_geom<16>(st.g, cta, ncta), smem, buf, cta, ncta); break;
-    case 8: gemv_post<8>(st.g, gemv_geom<8>(st.g, cta, ncta), smem, buf, cta, ncta); break;
-    default: gemv_post<4>(st.g, gemv_geom<4>(st.g, cta, ncta), smem, buf, cta, ncta); break;
-  }
-}
-
+template <int D>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams sp) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ StepStage s_stage[2];  // current and next stage parameters
+  __shared__ StepGemv s_g[2];        // GEMV parameters by ordinal parity
+  __shared__ AttnParams s_attn[2];   // attention parameters by ordinal parity
+  __shared__ int s_pos;
+  __shared__ uint64_t s_pre_bar;     // staging of a stage's masks / norm weights
   const unsigned cta = blockIdx.x, ncta = gridDim.x;
   const int tid = threadIdx.x;
+  unsigned char* act = smem_raw + sp.ring_bytes;
+  ProdDesc* s_desc = reinterpret_cast<ProdDesc*>(act + sp.act_bytes);  // [ngemv]
+  int* s_kind = reinterpret_cast<int*>(s_desc + sp.ngemv);               // [nstages]
 
-  auto load_stage = [&](int s, int slot) {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(sp.stages + s);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(&s_stage[slot]);
-    for (int i = tid; i < (int)(sizeof(StepStage) / 4); i += kStepThreads) dst[i] = src[i];
-  };
+  for (int s = tid; s < sp.nstages; s += kStepThreads) s_kind[s] = sp.kind[s];
+  for (int i = tid; i < sp.ngemv * (int)(sizeof(ProdDesc) / 16); i += kStepThreads)
+    reinterpret_cast<uint4*>(s_desc)[i] = __ldg(reinterpret_cast<const uint4*>(sp.desc) + i);
+  if (tid < kGemvWords && sp.ngemv > 0)
+    reinterpret_cast<uint32_t*>(&s_g[0])[tid] = reinterpret_cast<const uint32_t*>(sp.gemv)[tid];
+  if (tid < kAttnWords && sp.nattn > 0)
+    reinterpret_cast<uint32_t*>(&s_attn[0])[tid] = reinterpret_cast<const uint32_t*>(sp.attn)[tid];
+  if (tid == 0) mbar_init(&s_pre_bar, 1);
+  unsigned pre_uses = 0;  // phases of s_pre_bar started (uniform)
+  __syncthreads();
+  // Weights are constant: fill every warp's ring before waiting for the
+  // predecessor grid.
+  Ring R;
+  R.wring = smem_raw + (size_t)(tid >> 5) * D * kRingItemBytes;
+  R.cslot = 0;
+  R.P.n = -1;
+  R.P.t = R.P.t1 = 0;
+  R.P.slot = 0;
+  for (int i = 0; i < D; ++i) prod_next<D>(R.P, s_desc, sp.ngemv, R.wring, cta, ncta);
 
   grid_dep_wait();
   if (sp.trace != nullptr && cta == 0 && tid == 0) sp.trace[0] = global_timer_ns();
-  U32x8 buf[kStepU];
-  load_stage(0, 0);
+  // The token position is fixed for the whole step (the head advances it as
+  // the last thing the step does): read it once.
+  if (tid == 0) s_pos = (sp.pos != nullptr) ? (int)min((int64_t)0x7fffffff, max((int64_t)-1, *sp.pos)) : 0;
+  if (sp.nstages > 0 && s_kind[0] == kStageGemv) gemv_pre_smem(s_g[0], ncta, act, &s_pre_bar, pre_uses);
   __syncthreads();
-  if (s_stage[0].kind == kStageGemv) {
-    step_gemv_pre(s_stage[0], cta, ncta, smem_raw, buf);
-    __syncthreads();
-  }
+  int gn = 0, an = 0;  // ordinals of the next GEMV / attention stage
   for (int s = 0; s < sp.nstages; ++s) {
-    const int cur = s & 1, nxt = cur ^ 1;
-    const StepStage& st = s_stage[cur];
-    if (s + 1 < sp.nstages) load_stage(s + 1, nxt);  // read by the pre-barrier work below
-    if (st.kind == kStageGemv) {
-      step_gemv_post(st, cta, ncta, smem_raw, buf);
+    if (s_kind[s] == kStageGemv) {
+      // The next GEMV stage's parameters: loaded now, stored after this
+      // stage into the slot GEMV gn-1 used.
+      const bool more = gn + 1 < sp.ngemv;
+      uint32_t stash = 0u;
+      if (more && tid < kGemvWords) stash = __ldg(reinterpret_cast<const uint32_t*>(sp.gemv + gn + 1) + tid);
+      if (s + 1 < sp.nstages && s_kind[s + 1] == kStageAttn && an < sp.nattn)
+        attn_prefetch_l2(s_attn[an & 1], s_pos, cta, ncta);
+      run_gemv<D>(s_g[gn & 1], s_desc, sp.ngemv, cta, ncta, act, R, &s_pre_bar, pre_uses);
+      if (more && tid < kGemvWords) reinterpret_cast<uint32_t*>(&s_g[(gn + 1) & 1])[tid] = stash;
+      ++gn;
     } else {
-      // Latency-bound stage: meanwhile pull this CTA's rows of the following
-      // GEMV into L2 (HBM is otherwise idle).
-      __syncthreads();
-      if (s + 1 < sp.nstages && s_stage[nxt].kind == kStageGemv) step_gemv_l2_prefetch(s_stage[nxt], cta, ncta);
-      StepAttnSmem& S = *reinterpret_cast<StepAttnSmem*>(smem_raw);
-      for (int u = cta; u < st.units; u += ncta) {
-        attention_unit(st.a, u % st.a.splits, u / st.a.splits, S, sp.attn_part, sp.attn_count);
+      const bool more = an + 1 < sp.nattn;
+      uint32_t stash = 0u;
+      if (more && tid < kAttnWords) stash = __ldg(reinterpret_cast<const uint32_t*>(sp.attn + an + 1) + tid);
+      const AttnParams& a = s_attn[an & 1];
+      const int units = a.Hkv * a.splits;
+      StepAttnSmem& A = *reinterpret_cast<StepAttnSmem*>(act);
+      for (int u = cta; u < units; u += ncta) {
+        attention_unit(a, s_pos, u % a.splits, u / a.splits, A, sp.attn_part, sp.attn_count);
         __syncthreads();
       }
+      if (more && tid < kAttnWords) reinterpret_cast<uint32_t*>(&s_attn[(an + 1) & 1])[tid] = stash;
+      ++an;
     }
     unsigned long long* tr = sp.trace ? sp.trace + 1 + (size_t)s * (ncta + 1) : nullptr;
     if (tr != nullptr && tid == 0) tr[cta] = global_timer_ns();
     if (s + 1 < sp.nstages) {
-      grid_arrive(sp.bar_count);
-      if (s_stage[nxt].kind == kStageGemv) step_gemv_pre(s_stage[nxt], cta, ncta, smem_raw, buf);
-      if (!grid_wait(sp.bar_count, ncta, (unsigned)s)) return;
+      grid_arrive(sp.bar_count);  // includes __syncthreads: the stored parameters are visible
+      if (s_kind[s + 1] == kStageGemv) gemv_pre_smem(s_g[gn & 1], ncta, act, &s_pre_bar, pre_uses);
+      if (!grid_wait(sp.bar_count, ncta, (unsigned)s)) {
+        // No copy may land after exit.
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        if (tid == 0 && pre_uses > 0u) mbar_wait_bounded(&s_pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);
+        __syncthreads();
+        return;
+      }
       if (tr != nullptr && cta == 0 && tid == 0) tr[ncta] = global_timer_ns();
     }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   step_exit(sp.bar_count, sp.bar_exit, ncta);
   grid_dep_launch_dependents();
 }
+
+// Ring depths the persistent kernel is built for (the host takes the largest
+// whose rings fit next to the step's working set).
+#ifndef NMS_STEP_DEPTH_HI
+#define NMS_STEP_DEPTH_HI 10
+#define NMS_STEP_DEPTH_LO 6
+#endif
+constexpr int kStepDepthHi = NMS_STEP_DEPTH_HI;
+constexpr int kStepDepthLo = NMS_STEP_DEPTH_LO;
 
 }  // namespace nms
