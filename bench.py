@@ -1,6 +1,6 @@
 """Benchmark: batch-1 decode ms/token under a CUDA graph (the reference's
-headline metric), with the sparse GEMV's achieved HBM bandwidth as the
-roofline of the dominant kernel.
+headline metric), with the dominant kernel's achieved HBM bandwidth as its
+roofline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--model llama-3.1-8b] [--nm 32:64] [--ctx 512]
@@ -20,9 +20,11 @@ The JSON line also carries:
   e2e          the same metric through the public generation API with a
                pinned host->device token copy and a device->host read of the
                next token every step (positions advance);
-  roofline     the sparse GEMV kernel timed live in a plan holding only the
-               step's GEMV launches: algorithmic bytes / duration vs the
-               measured HBM copy bandwidth (MEASURED_PEAKS.json);
+  roofline     the dominant kernel of the timed region -- the persistent
+               decode_step_kernel (one launch = one step): the step's
+               algorithmic bytes / replay time vs the measured HBM copy
+               bandwidth (MEASURED_PEAKS.json); gemv_roofline: the sparse
+               GEMV kernel alone, timed live in a plan of the step's GEMVs;
   cpu_baseline the reference's torch CPU path (dense masked fp16 F.linear)
                on a bounded sample of the same workload, on this host;
   dense        the same engine with dense weights, and dense cuBLAS decode
@@ -75,7 +77,33 @@ def parse_args():
     p.add_argument("--mode", choices=["auto", "persistent", "plan"], default="auto",
                    help="decode-step executor: one persistent kernel or a per-kernel launch plan")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--layers", type=int, default=0,
+                   help="profiling only: keep the model's shapes but this many decoder layers")
+    p.add_argument("--vocab", type=int, default=0, help="profiling only: override the vocabulary size")
     return p.parse_args()
+
+
+def model_config(args):
+    """The named configuration, with the profiling-only layer / vocabulary
+    overrides applied."""
+    import dataclasses
+
+    from spmv_decode_b200.model import ModelArgs
+
+    cfg = ModelArgs.from_name(args.model)
+    over = {}
+    if args.layers:
+        over["n_layer"] = args.layers
+    if args.vocab:
+        over["vocab_size"] = args.vocab
+    return dataclasses.replace(cfg, **over) if over else cfg
+
+
+def workload_name(args) -> str:
+    w = f"{args.model}-arch {args.nm} decode, ctx {args.ctx}, batch 1"
+    if args.layers or args.vocab:
+        w += f" [profiling case: {args.layers or 'all'} layers, vocab {args.vocab or 'full'}]"
+    return w
 
 
 def measured_peaks() -> dict:
@@ -86,13 +114,14 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def profiled_traffic(workload: str):
-    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
-    f = ROOT / "profiles" / "gemv_traffic.json"
+def profiled_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch of `kernel` on `workload` from the committed ncu
+    summary (profiles/traffic.json), if any."""
+    f = ROOT / "profiles" / "traffic.json"
     if not f.exists():
         return None
     d = json.loads(f.read_text())
-    return d.get(workload)
+    return d.get(kernel, {}).get(workload)
 
 
 class ClockSampler:
@@ -172,7 +201,7 @@ def run_reference_arm(args, world: int, rank: int) -> None:
     from oracle.decode_oracle import cpu_decode_sample
     from spmv_decode_b200.model import ModelArgs
 
-    cfg = ModelArgs.from_name(args.model)
+    cfg = model_config(args)
     nm = None if args.nm == "dense" else tuple(int(v) for v in args.nm.split(":"))
     threads = os.cpu_count() or 1
     # Each "step" is one sampled token; keep the run bounded.
@@ -185,7 +214,7 @@ def run_reference_arm(args, world: int, rank: int) -> None:
         "warmup": 1, "ms_per_step": round(v, 3), "higher_is_better": False, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16 (torch CPU F.linear)", "data": "synthetic random-init weights",
         "impl": "reference",
-        "config": {"workload": f"{args.model}-arch {args.nm} decode, ctx {args.ctx}, batch 1",
+        "config": {"workload": workload_name(args),
                    "model": args.model, "nm": args.nm, "ctx": args.ctx, "parallelism": "cpu"},
         "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": r["threads"], "kind": "port",
                          "sample": r["sample"]},
@@ -217,7 +246,7 @@ def main():
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     nm = None if args.nm == "dense" else tuple(int(v) for v in args.nm.split(":"))
-    cfg = ModelArgs.from_name(args.model)
+    cfg = model_config(args)
     max_seq = args.ctx + 1 + args.e2e_steps + 8
     t_build = time.time()
     tp = None
@@ -299,15 +328,28 @@ def main():
     _lib.lib().nms_plan_destroy(plan)
     peaks = measured_peaks()
     achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
-    workload = f"{args.model}-arch {args.nm} decode, ctx {args.ctx}, batch 1"
-    roofline = {"bound": "hbm", "kernel": "gemv_packed_kernel", "achieved": round(achieved, 1),
-                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "peak_source": peaks["source"], "traffic": profiled_traffic(workload),
-                "algorithmic_bytes_per_step": gemv_bytes, "launches_per_step": n_gemv,
-                "mean_launch_us": round(gemv_ms * 1e3 / n_gemv, 3)}
-    weight_bytes = sum(r["bytes"] for r in eng.gemv_records)  # incl. head
-    step_roofline = {"bytes_per_token": weight_bytes, "ideal_ms": round(weight_bytes / peaks["hbm_gbs"] / 1e6, 4),
-                     "frac": round(weight_bytes / peaks["hbm_gbs"] / 1e6 / ms, 4)}
+    workload = workload_name(args)
+    gemv_roofline = {"bound": "hbm", "kernel": "gemv_packed_kernel", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "traffic": profiled_traffic("gemv_packed_kernel", workload),
+                     "algorithmic_bytes": gemv_bytes, "launches": n_gemv,
+                     "mean_launch_us": round(gemv_ms * 1e3 / n_gemv, 3),
+                     "note": "the step's GEMV launches alone (plan executor), timed in their own CUDA graph"}
+    sb = eng.step_bytes(args.ctx)
+    # The dominant kernel of the timed region: with the persistent executor
+    # the whole step is one decode_step_kernel launch, so its duration is the
+    # replay time; with the plan executor the GEMV kernel above dominates.
+    if engine_mode == "persistent":
+        step_achieved = sb["total"] / (ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "decode_step_kernel", "achieved": round(step_achieved, 1),
+                    "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(step_achieved / peaks["hbm_gbs"], 4),
+                    "peak_source": peaks["source"], "traffic": profiled_traffic("decode_step_kernel", workload),
+                    "algorithmic_bytes": sb["total"], "launches": 1, "mean_launch_us": round(ms * 1e3, 3)}
+    else:
+        roofline = dict(gemv_roofline)
+        roofline.pop("note")
+    step_roofline = {"bytes_per_token": sb, "ideal_ms": round(sb["total"] / peaks["hbm_gbs"] / 1e6, 4),
+                     "frac": round(sb["total"] / peaks["hbm_gbs"] / 1e6 / ms, 4)}
     del g2, graph, gd
     eng.close()
     del eng
@@ -380,6 +422,7 @@ def main():
             "e2e": {"value": round(e2e_ms, 4), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
                     "steps": e2e_steps, "note": "public generation API, host token in/out every step"},
             "roofline": roofline,
+            "gemv_roofline": gemv_roofline,
             "step_roofline": step_roofline,
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,

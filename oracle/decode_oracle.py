@@ -137,12 +137,17 @@ class OracleModel:
             self.head = self.head.float()
         self.k = [torch.zeros(n_kv, max_seq, head_dim, dtype=torch.float16) for _ in layers]
         self.v = [torch.zeros(n_kv, max_seq, head_dim, dtype=torch.float16) for _ in layers]
+        # Tensor-parallel shard: sums the fp16 partial o- and down-projection
+        # outputs over the ranks (identity on one rank).
+        self.reduce = None
 
     # -- construction --------------------------------------------------------
     @classmethod
-    def from_transformer(cls, model, max_seq: Optional[int] = None, linear_dtype=torch.float32):
+    def from_transformer(cls, model, max_seq: Optional[int] = None, linear_dtype=torch.float32,
+                         heads: Optional[tuple] = None):
         """Copy the weights of a spmv_decode_b200 Transformer (sparse linears
-        expanded to masked dense matrices via their reference-layout values)."""
+        expanded to masked dense matrices via their reference-layout values).
+        ``heads`` = (query heads, KV heads) of a tensor-parallel shard."""
         c = model.config
 
         def dense(lin):
@@ -169,7 +174,8 @@ class OracleModel:
         S = max_seq or 64
         return cls(layers=layers, emb=model.tok_embeddings.weight.detach().cpu().half(),
                    head=model.output_weight.detach().cpu().half(), final_norm=model.norm.weight.detach().cpu().half(),
-                   n_head=c.n_head, n_kv=c.n_local_heads, head_dim=c.head_dim, eps=c.norm_eps,
+                   n_head=heads[0] if heads else c.n_head, n_kv=heads[1] if heads else c.n_local_heads,
+                   head_dim=c.head_dim, eps=c.norm_eps,
                    rope=rope_table(max(S, 8), c.head_dim, c.rope_base, c.rope_scaling, c.rope_style),
                    style=c.rope_style, max_seq=S, linear_dtype=linear_dtype)
 
@@ -246,12 +252,18 @@ class OracleModel:
             s = torch.einsum("hgd,hpd->hgp", qf, Kc) / math.sqrt(D)
             p = torch.softmax(s, dim=-1)
             y = torch.einsum("hgp,hpd->hgd", p, Vc).reshape(Hq * D).to(torch.float16)
-            x = x + self._linear(L.wo, y)
+            o = self._linear(L.wo, y)
+            if self.reduce is not None:
+                o = self.reduce(o)
+            x = x + o
             hn = rmsnorm(x, L.norm2, self.eps)
             g = self._linear(L.gate, hn)
             u = self._linear(L.up, hn)
             act = torch.nn.functional.silu(g.float()).to(torch.float16) * u
-            x = x + self._linear(L.down, act)
+            dn = self._linear(L.down, act)
+            if self.reduce is not None:
+                dn = self.reduce(dn)
+            x = x + dn
         xn = rmsnorm(x, self.final_norm, self.eps)
         return self._linear(self.head, xn)
 

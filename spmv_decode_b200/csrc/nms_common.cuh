@@ -130,7 +130,7 @@ __device__ __forceinline__ void fma2_f32_f16_bcast(float& acc0, float& acc1, uin
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk global->shared copy (TMA, non-tensor, no multicast).
+// mbarrier + bulk global->shared copy (TMA, non-tensor, this CTA only).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -59,7 +59,7 @@ class DecodeEngine:
     def __init__(self, model: Transformer, max_seq_length: int, *, pdl: bool = True, prefetch_bytes: int = 0,
                  next_prefetch_bytes: int = 0, attn_splits: int = 0, history_len: int = 0, mode: str = "auto",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None, tp_rank: int = 0, tp_size: int = 1,
-                 local_heads: Optional[tuple] = None):
+                 local_heads: Optional[tuple] = None, head_hook: Optional[Callable[[bool], None]] = None):
         c = model.config
         self.config = c
         self.model = model
@@ -71,6 +71,9 @@ class DecodeEngine:
         self.prefetch_bytes = int(prefetch_bytes)  # per-warp L2 look-ahead inside a GEMV
         self.next_prefetch_bytes = int(next_prefetch_bytes)  # L2 prefetch of the following GEMV's weights
         self.allreduce = allreduce
+        # Tensor parallelism: after the (non-advancing) local head, head_hook(advance)
+        # turns the rank's argmax into the global greedy token.
+        self.head_hook = head_hook
         if mode not in ("auto", "persistent", "plan"):
             raise ValueError(f"unknown mode {mode!r}")
         self.tp_rank, self.tp_size = tp_rank, tp_size
@@ -121,7 +124,7 @@ class DecodeEngine:
             self._build(model, attn_splits)
             self._steps = {}
             self.mode = "plan"
-            if mode != "plan" and allreduce is None:
+            if mode != "plan" and allreduce is None and head_hook is None:
                 try:
                     fixed = list(range(self._head_index)) + [self._head_index]
                     adv = list(range(self._head_index)) + [self._head_index + 1]
@@ -197,6 +200,17 @@ class DecodeEngine:
         if not argmax or not advance:
             self.gemv_records.append(dict(args=a, bytes=bytes_, dense=s0["dense"], argmax=argmax,
                                           shape=(sum(s["rows"] for s in segs), s0["K"])))
+
+    def step_bytes(self, ctx: int) -> dict:
+        """Algorithmic HBM bytes of one decode step at context length `ctx`:
+        every GEMV's kept weights, mask offsets, input and output vectors
+        (the head once), plus the attention's K/V reads of `ctx` cached
+        positions and its K/V writes of the new one, per layer."""
+        gemv = sum(r["bytes"] for r in self.gemv_records)
+        layers = self.config.n_layer
+        kv_read = layers * 2 * self.Hkv * ctx * self.D * 2
+        kv_write = layers * 2 * self.Hkv * self.D * 2
+        return {"gemv": gemv, "kv": kv_read + kv_write, "total": gemv + kv_read + kv_write}
 
     def gemv_plan(self, include_head: bool = False):
         """A separate plan holding only this step's GEMV launches (same
@@ -318,11 +332,15 @@ class DecodeEngine:
             # after the down-projection (partial y_down) of every layer.
             for i, cut in enumerate(self.cut_points):
                 self._launch(begin, cut, stream)
-                self.allreduce(self.y_o if i % 2 == 0 else self.y_down)
+                with torch.cuda.stream(stream):
+                    self.allreduce(self.y_o if i % 2 == 0 else self.y_down)
                 begin = cut
-        head = self._head_index + (1 if advance else 0)
+        head = self._head_index + (1 if advance and self.head_hook is None else 0)
         self._launch(begin, self._head_index, stream)
         self._launch(head, head + 1, stream)
+        if self.head_hook is not None:
+            with torch.cuda.stream(stream):
+                self.head_hook(advance)
 
     def reset(self) -> None:
         self.k_cache.zero_()
