@@ -412,7 +412,7 @@ def main():
         line = {
             "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None if pub is None else round(ms / pub[0], 4),
+            "vs_baseline": None if (pub is None or args.layers or args.vocab) else round(ms / pub[0], 4),
             "dtype": "f16 (fp32 accumulate)",
             "data": "synthetic: random-init weights N(0,0.02), KV cache N(0,0.02) (reference fixed-context protocol)",
             "config": {"workload": workload, "model": args.model, "nm": args.nm, "ctx": args.ctx,
