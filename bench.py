@@ -255,7 +255,7 @@ def main():
 
         eng, tp = build_tp_engine(cfg, nm, world, rank, dev, max_seq=max_seq, seed=args.seed,
                                   prefetch_bytes=args.prefetch, next_prefetch_bytes=args.next_prefetch,
-                                  history_len=max_seq)
+                                  history_len=max_seq, mode=args.mode)
     else:
         model = build_model(cfg, nm=nm, device=dev, seed=args.seed, init="device")
         eng = DecodeEngine(model, max_seq, prefetch_bytes=args.prefetch, next_prefetch_bytes=args.next_prefetch,
@@ -273,7 +273,7 @@ def main():
     assert torch.isfinite(eng.logits.float()).all(), "non-finite logits after replay"
     # Kernels of this library per step: one persistent kernel, or the plan's
     # launches (the plan holds the head twice: fixed and advancing variants).
-    launches_per_step = 1 if eng.mode == "persistent" else eng.size() - 1
+    launches_per_step = {"persistent": 1, "persistent_tp": 2}.get(eng.mode, eng.size() - 1)
     engine_mode = eng.mode
     dev_err = _lib.device_error()
 
@@ -339,11 +339,13 @@ def main():
     # The dominant kernel of the timed region: with the persistent executor
     # the whole step is one decode_step_kernel launch, so its duration is the
     # replay time; with the plan executor the GEMV kernel above dominates.
-    if engine_mode == "persistent":
+    if engine_mode in ("persistent", "persistent_tp"):
         step_achieved = sb["total"] / (ms * 1e-3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "decode_step_kernel", "achieved": round(step_achieved, 1),
+        kname = "decode_step_kernel" if engine_mode == "persistent" else "decode_step_kernel (+ head GEMV, NCCL argmax)"
+        roofline = {"bound": "hbm", "kernel": kname, "achieved": round(step_achieved, 1),
                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(step_achieved / peaks["hbm_gbs"], 4),
-                    "peak_source": peaks["source"], "traffic": profiled_traffic("decode_step_kernel", workload),
+                    "peak_source": peaks["source"],
+                    "traffic": profiled_traffic("decode_step_kernel", workload) if world == 1 else None,
                     "algorithmic_bytes": sb["total"], "launches": 1, "mean_launch_us": round(ms * 1e3, 3)}
     else:
         roofline = dict(gemv_roofline)
@@ -435,6 +437,7 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        tp.close()
         del tp
         dist.destroy_process_group()
 

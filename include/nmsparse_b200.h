@@ -244,10 +244,11 @@ int nms_plan_launch(const nms_plan* plan, int32_t begin, int32_t end, void* stre
 /* ---------------------------------------------------------------------------
  * Persistent decode step: the GEMV and attention records listed in
  * `records` (plan indices, in execution order) run as stages of ONE
- * cooperative kernel (one 1024-thread CTA per SM) separated by in-kernel grid
- * barriers; each CTA issues the next GEMV stage's first weight loads before
- * it waits at a barrier.  Replaces the per-kernel decode step of the plan
- * (and, like it, the reference's compiled + graph-captured decode_one_token).
+ * cooperative kernel (one 512-thread CTA per SM) separated by in-kernel grid
+ * barriers; every warp streams its weights through a shared-memory ring whose
+ * copies run ahead across stage boundaries.  Replaces the per-kernel decode
+ * step of the plan (and, like it, the reference's compiled + graph-captured
+ * decode_one_token).
  * Records other than GEMV and attention (embedding, pack) return
  * NMS_ERR_NOT_IMPLEMENTED, and the plan path is used.  nms_step_create
  * allocates the stage table and barrier/attention scratch once (device
@@ -266,6 +267,41 @@ int nms_step_info(const nms_step* step, int32_t* nstages, int32_t* grid);
  * work of stage s; buf[1 + s*(grid+1) + grid] = when CTA 0 left the barrier
  * after stage s.  Needs 1 + nstages*(grid+1) uint64 entries (device memory). */
 int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel persistent step (no reference counterpart: the reference
+ * decodes on one GPU; replaces the NCCL all-reduce after o_proj / down_proj
+ * that a gpt-fast tp.py would add).  One process per GPU.  Each rank
+ * allocates an exchange area with nms_ipc_alloc, the ranks swap the 64-byte
+ * handles (e.g. torch.distributed all_gather_object) and open each other's
+ * areas with nms_ipc_open.  nms_step_set_tp then turns the GEMV stages listed
+ * in `reduce_stages` (stage indices of the step, ascending: the row-parallel
+ * o- and down-projections) into exchange points: every CTA writes its fp32
+ * partial rows into every rank's area over NVLink, each as one 8-byte
+ * {value, tag} store whose tag names the step and point, so the data are
+ * their own arrival signal; the next GEMV stage adds the ranks' partials
+ * (rank order, identical on every rank) in place of its residual addend;
+ * after a final exchange point the reduced vector is also written to that
+ * stage's output.  Waits are bounded (device error 3).  Area layout: step
+ * counter (8 bytes, padded to 256) + nreduce x world x dim {fp32, u32 tag}.
+ * ------------------------------------------------------------------------- */
+#define NMS_MAX_TP 8
+typedef struct nms_tp_config {
+  int32_t world, rank;
+  int32_t dim;                   /* length of every reduced vector */
+  int32_t pad_;
+  void* area[NMS_MAX_TP];        /* every rank's exchange area, as mapped in this process */
+} nms_tp_config;
+
+/* Bytes of an exchange area for `nreduce` points of `dim` values over `world` ranks. */
+int64_t nms_tp_area_bytes(int32_t nreduce, int32_t world, int32_t dim);
+/* cudaMalloc'd, zeroed device memory and its IPC handle (64 bytes). */
+int nms_ipc_alloc(int64_t bytes, void** ptr_out, void* handle_out);
+int nms_ipc_free(void* ptr);
+/* Map another process's allocation (its 64-byte handle) into this one. */
+int nms_ipc_open(const void* handle, void** ptr_out);
+int nms_ipc_close(void* ptr);
+int nms_step_set_tp(nms_step* step, const int32_t* reduce_stages, int32_t nreduce, const nms_tp_config* cfg);
 
 #ifdef __cplusplus
 }

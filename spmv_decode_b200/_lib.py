@@ -61,7 +61,23 @@ EXPORTED_SYMBOLS = (
     "nms_step_destroy",
     "nms_step_info",
     "nms_step_set_trace",
+    "nms_tp_area_bytes",
+    "nms_ipc_alloc",
+    "nms_ipc_free",
+    "nms_ipc_open",
+    "nms_ipc_close",
+    "nms_step_set_tp",
 )
+
+NMS_MAX_TP = 8
+
+
+class NmsTpConfig(ctypes.Structure):
+    """nms_tp_config (include/nmsparse_b200.h)."""
+
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("dim", ctypes.c_int32),
+                ("pad_", ctypes.c_int32), ("area", ctypes.c_void_p * NMS_MAX_TP)]
+
 
 c_void_p = ctypes.c_void_p
 c_i32 = ctypes.c_int32
@@ -166,6 +182,12 @@ def _declare(lib: ctypes.CDLL) -> None:
         "nms_step_destroy": (I32, [P]),
         "nms_step_info": (I32, [P, ctypes.POINTER(I32), ctypes.POINTER(I32)]),
         "nms_step_set_trace": (I32, [P, P, I64]),
+        "nms_tp_area_bytes": (I64, [I32, I32, I32]),
+        "nms_ipc_alloc": (I32, [I64, ctypes.POINTER(P), P]),
+        "nms_ipc_free": (I32, [P]),
+        "nms_ipc_open": (I32, [P, ctypes.POINTER(P)]),
+        "nms_ipc_close": (I32, [P]),
+        "nms_step_set_tp": (I32, [P, ctypes.POINTER(I32), I32, ctypes.POINTER(NmsTpConfig)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -486,6 +486,8 @@ struct nms_step {
   int grid = 0;
   size_t smem = 0;
   int depth = 0;            // weight-ring depth (selects the kernel instantiation)
+  std::vector<nms::StepGemv> gemvs;    // host copy of the device GEMV stage table
+  std::vector<int32_t> gemv_of_stage;  // stage -> GEMV ordinal (-1: attention)
   void* dev_mem = nullptr;  // stage tables | barrier words | attention partials | head counters
   nms::StepParams params;
 };
@@ -775,6 +777,7 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
       memset(&sg, 0, sizeof(sg));
       sg.g = r.gp;
       sg.lanes = nms::ring_lanes(sg.g.w_pad);
+      sg.tp_send = sg.tp_recv = -1;
       const int RG = 32 / sg.lanes;
       sg.g.row_groups = (sg.g.rows_total + RG - 1) / RG;
       if (sg.g.epilogue == nms::kEpiArgmax && (sg.g.amax_val == nullptr || grid > r.amax_capacity))
@@ -860,6 +863,7 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
   st->smem = smem;
   st->depth = depth;
   nms::StepParams& P = st->params;
+  memset(&P, 0, sizeof(P));
   P.kind = reinterpret_cast<const int32_t*>(base + kind_off);
   P.gemv = reinterpret_cast<const nms::StepGemv*>(base + gemv_off);
   P.desc = reinterpret_cast<const nms::ProdDesc*>(base + desc_off);
@@ -875,7 +879,108 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
   P.attn_count = reinterpret_cast<unsigned*>(base + cnt_off);
   P.trace = nullptr;
   P.pos = pos_ptr;
+  P.tp_world = 1;
+  st->gemvs = gemvs;
+  st->gemv_of_stage.assign(kinds.size(), -1);
+  for (size_t k = 0, g = 0; k < kinds.size(); ++k)
+    if (kinds[k] == nms::kStageGemv) st->gemv_of_stage[k] = (int32_t)g++;
   *out = st;
+  return NMS_OK;
+}
+
+int64_t nms_tp_area_bytes(int32_t nreduce, int32_t world, int32_t dim) {
+  if (nreduce < 1 || world < 1 || dim < 1) return -1;
+  return 256 + (int64_t)nreduce * world * dim * 8;
+}
+
+int nms_ipc_alloc(int64_t bytes, void** ptr_out, void* handle_out) {
+  if (bytes <= 0 || ptr_out == nullptr || handle_out == nullptr) return fail(NMS_ERR_VALUE, "bad argument");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return fail_cuda(e, "exchange area allocation");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+  memcpy(handle_out, &h, sizeof(h));
+  *ptr_out = p;
+  return NMS_OK;
+}
+
+int nms_ipc_free(void* ptr) {
+  if (ptr == nullptr) return NMS_OK;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? NMS_OK : fail_cuda(e, "cudaFree");
+}
+
+int nms_ipc_open(const void* handle, void** ptr_out) {
+  if (handle == nullptr || ptr_out == nullptr) return fail(NMS_ERR_VALUE, "bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? NMS_OK : fail_cuda(e, "cudaIpcOpenMemHandle");
+}
+
+int nms_ipc_close(void* ptr) {
+  if (ptr == nullptr) return NMS_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? NMS_OK : fail_cuda(e, "cudaIpcCloseMemHandle");
+}
+
+int nms_step_set_tp(nms_step* step, const int32_t* reduce_stages, int32_t nreduce, const nms_tp_config* cfg) {
+  if (step == nullptr || reduce_stages == nullptr || cfg == nullptr) return fail(NMS_ERR_VALUE, "null argument");
+  if (cfg->world < 2 || cfg->world > NMS_MAX_TP || cfg->rank < 0 || cfg->rank >= cfg->world)
+    return fail(NMS_ERR_VALUE, "world=%d rank=%d (2 <= world <= %d)", cfg->world, cfg->rank, NMS_MAX_TP);
+  if (nreduce < 1 || cfg->dim < 1) return fail(NMS_ERR_VALUE, "nreduce=%d dim=%d", nreduce, cfg->dim);
+  for (int r = 0; r < cfg->world; ++r)
+    if (cfg->area[r] == nullptr || !aligned(cfg->area[r], 256)) return fail(NMS_ERR_VALUE, "area %d missing or unaligned", r);
+  std::vector<nms::StepGemv> g = step->gemvs;
+  for (nms::StepGemv& sg : g) sg.tp_send = sg.tp_recv = -1;
+  int last = -1;
+  for (int j = 0; j < nreduce; ++j) {
+    const int s = reduce_stages[j];
+    if (s <= last || s >= step->nstages) return fail(NMS_ERR_VALUE, "reduce stages must ascend inside the step");
+    last = s;
+    const int gi = step->gemv_of_stage[s];
+    if (gi < 0) return fail(NMS_ERR_VALUE, "stage %d is not a GEMV", s);
+    nms::StepGemv& snd = g[gi];
+    if (snd.g.epilogue != nms::kEpiStore || snd.g.mode == nms::kModePaired || snd.g.rows_total != cfg->dim)
+      return fail(NMS_ERR_VALUE, "stage %d: an exchange point must store %d rows", s, cfg->dim);
+    snd.tp_send = j;
+    // The next GEMV stage adds the reduced vector as its residual addend.
+    for (int k = s + 1; k < step->nstages; ++k) {
+      const int gk = step->gemv_of_stage[k];
+      if (gk < 0) continue;
+      nms::StepGemv& rcv = g[gk];
+      if (rcv.g.prologue != nms::kProResidNorm || rcv.g.x2 != snd.g.out || rcv.g.K != cfg->dim)
+        return fail(NMS_ERR_VALUE, "stage %d: the GEMV after exchange point %d must take it as residual addend", k, j);
+      rcv.tp_recv = j;
+      break;
+    }
+  }
+  const size_t cbytes = 256;  // the step counter, then the values
+  nms::StepParams& P = step->params;
+  cudaError_t e = cudaSetDevice(step->device);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(const_cast<nms::StepGemv*>(P.gemv), g.data(), g.size() * sizeof(nms::StepGemv),
+                   cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return fail_cuda(e, "tensor-parallel stage table");
+  P.tp_world = cfg->world;
+  P.tp_rank = cfg->rank;
+  P.tp_dim = cfg->dim;
+  P.tp_nreduce = nreduce;
+  for (int r = 0; r < nms::kMaxTp; ++r) {
+    unsigned char* a = r < cfg->world ? static_cast<unsigned char*>(cfg->area[r]) : nullptr;
+    // area: [steps completed] (padded to 256 bytes), then {fp32, tag} values
+    P.tp_vals[r] = a ? reinterpret_cast<uint2*>(a + cbytes) : nullptr;
+  }
+  unsigned char* mine = static_cast<unsigned char*>(cfg->area[cfg->rank]);
+  P.tp_epoch = reinterpret_cast<unsigned long long*>(mine);
+  P.tp_my_vals = reinterpret_cast<const uint2*>(mine + cbytes);
+  step->gemvs = g;
   return NMS_OK;
 }
 

@@ -36,6 +36,7 @@ constexpr uint64_t kBarrierLimitNs = 200ull * 1000 * 1000;
 constexpr int kMaxSplits = 16;  // attention splits per KV head (cluster-size bound of the standalone kernel)
 
 enum StageKind : int32_t { kStageGemv = 0, kStageAttn = 1 };
+constexpr int kMaxTp = 8;
 
 struct StepGemv;
 struct ProdDesc;
@@ -57,6 +58,13 @@ struct StepParams {
   // trace[1 + s*(ncta+1) + ncta] = time CTA 0 left the barrier after stage s.
   unsigned long long* trace;
   const int64_t* pos;       // token position of the step (all attention stages)
+  // Tensor parallelism (tp_world > 1): exchange areas of every rank as
+  // mapped in this process (values[nreduce][world][dim] of {fp32, tag}),
+  // this rank's own area, and the local count of completed steps.
+  int32_t tp_world, tp_rank, tp_dim, tp_nreduce;
+  uint2* tp_vals[kMaxTp];
+  const uint2* tp_my_vals;
+  unsigned long long* tp_epoch;
 };
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -106,7 +114,8 @@ __device__ __forceinline__ bool grid_wait(const unsigned* count, unsigned ncta, 
 
 // Called once by every CTA as it leaves: the last one resets the barrier
 // counter (no CTA of this launch reads it any more).
-__device__ __forceinline__ void step_exit(unsigned* count, unsigned* exit_count, unsigned ncta) {
+__device__ __forceinline__ void step_exit(unsigned* count, unsigned* exit_count, unsigned ncta,
+                                          unsigned long long* epoch) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -114,8 +123,64 @@ __device__ __forceinline__ void step_exit(unsigned* count, unsigned* exit_count,
     if (prev == ncta - 1) {
       atomicExch(count, 0u);
       atomicExch(exit_count, 0u);
+      if (epoch != nullptr) atomicAdd(epoch, 1ull);  // steps completed (tensor-parallel exchange targets)
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel exchange (one process per GPU, peers' areas mapped over
+// NVLink).  Exchange point j of step e: every CTA of every rank writes each of
+// its partial rows into slot [j][its rank] of every rank's area as ONE 8-byte
+// store {fp32 value, tag}, tag = e * nreduce + j + 1 (never 0, the area
+// starts zeroed).  An 8-byte store lands whole, so a reader that sees the
+// expected tag sees the value: the data are their own arrival signal -- no
+// fence, counter or cross-GPU barrier.  Readers (the next stage's prologue)
+// poll each word they add.  Slots are reused one step later; a rank cannot
+// reach step e + 1's point j before every rank has contributed to -- and so
+// finished reading -- step e's points up to the last one.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t tp_tag(const StepParams& sp, unsigned long long epoch, int j) {
+  return (uint32_t)(epoch * (unsigned long long)sp.tp_nreduce + (unsigned long long)j + 1ull);
+}
+
+__device__ __forceinline__ void tp_put(uint2* dst, float v, uint32_t tag) {
+  asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(dst), "r"(__float_as_uint(v)), "r"(tag)
+               : "memory");
+}
+
+__device__ __forceinline__ uint2 tp_get(const uint2* src) {
+  uint2 w;
+  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(src) : "memory");
+  return w;
+}
+
+// Sum of exchange point j's partials for element i, in rank order (the same
+// on every rank).  A word whose tag has not arrived is polled (bounded; after
+// a recorded device error nobody waits any more).
+__device__ __noinline__ uint2 tp_poll(const uint2* src, uint32_t tag) {
+  uint2 w = tp_get(src);
+  const uint64_t t0 = global_timer_ns();
+  while (w.y != tag) {
+    if (*reinterpret_cast<volatile int*>(&g_device_error) != 0) break;
+    if (global_timer_ns() - t0 > kBarrierLimitNs) {
+      set_device_error(kDevBarrierTimeout);
+      break;
+    }
+    w = tp_get(src);
+  }
+  return w;
+}
+
+__device__ __forceinline__ float tp_sum(const StepParams& sp, int j, int i, uint32_t tag) {
+  const uint2* v = sp.tp_my_vals + (size_t)j * sp.tp_world * sp.tp_dim + i;
+  float acc = 0.f;
+  for (int r = 0; r < sp.tp_world; ++r) {
+    uint2 w = tp_get(v + (size_t)r * sp.tp_dim);
+    if (w.y != tag) w = tp_poll(v + (size_t)r * sp.tp_dim, tag);
+    acc += __uint_as_float(w.x);
+  }
+  return acc;
 }
 
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src) {
@@ -147,8 +212,10 @@ constexpr uint64_t kPreWaitLimitNs = 200ull * 1000 * 1000;
 
 struct StepGemv {
   GemvParams g;
-  int32_t lanes;  // L: lanes per row (32, 16, 8 or 4), w_pad % (16 L) == 0
-  int32_t pad_[3];
+  int32_t lanes;    // L: lanes per row (32, 16, 8 or 4), w_pad % (16 L) == 0
+  int32_t tp_send;  // tensor parallel: exchange point this stage's partial rows go to (-1: none)
+  int32_t tp_recv;  // exchange point whose summed partials replace this stage's residual addend (-1: none)
+  int32_t pad_;
 };
 
 // What the producer needs of a GEMV stage (64 bytes, all stages resident).
@@ -374,9 +441,9 @@ __device__ __forceinline__ void gemv_pre_smem(const StepGemv& sg, unsigned ncta,
 // statistic), gather, this warp's items from its ring (each consumed item
 // commits the warp's next copy), epilogue.
 template <int L, int D>
-__device__ __forceinline__ void gemv_stage(const StepGemv& sg, const ProdDesc* descs, int ngemv, unsigned cta,
-                                           unsigned ncta, unsigned char* act, Ring& R, uint64_t* pre_bar,
-                                           unsigned pre_uses) {
+__device__ __forceinline__ void gemv_stage(const StepParams& sp, const StepGemv& sg, const ProdDesc* descs, int ngemv,
+                                           unsigned cta, unsigned ncta, unsigned char* act, Ring& R,
+                                           uint64_t* pre_bar, unsigned pre_uses, unsigned long long epoch) {
   constexpr int RG = kWarp / L, NT = kStepThreads, CB = 32 * L;
   const GemvParams& p = sg.g;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -392,13 +459,21 @@ __device__ __forceinline__ void gemv_stage(const StepGemv& sg, const ProdDesc* d
   const __half* xsrc = input_row(p);
   const bool resid = (p.prologue == kProResidNorm);
   const bool add = resid && (p.x2 != nullptr);
+  const int tpj = sg.tp_recv;  // >= 0: the addend is the sum of the ranks' partials
+  const uint32_t rtag = tpj >= 0 ? tp_tag(sp, epoch, tpj) : 0u;
   float ss = 0.f;
   if ((p.K & 7) == 0 && (reinterpret_cast<uintptr_t>(xsrc) & 15u) == 0 &&
       (!add || (reinterpret_cast<uintptr_t>(p.x2) & 15u) == 0)) {
     for (int i8 = tid; i8 < p.K / 8; i8 += NT) {
       const uint4 a = *reinterpret_cast<const uint4*>(xsrc + (size_t)i8 * 8);
       uint4 b = make_uint4(0u, 0u, 0u, 0u);
-      if (add) b = *reinterpret_cast<const uint4*>(p.x2 + (size_t)i8 * 8);
+      if (add && tpj >= 0) {
+        __half* bw = reinterpret_cast<__half*>(&b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bw[e] = f2h(tp_sum(sp, tpj, i8 * 8 + e, rtag));
+      } else if (add) {
+        b = *reinterpret_cast<const uint4*>(p.x2 + (size_t)i8 * 8);
+      }
       const __half* ah = reinterpret_cast<const __half*>(&a);
       const __half* bh = reinterpret_cast<const __half*>(&b);
       uint4 o;
@@ -414,7 +489,7 @@ __device__ __forceinline__ void gemv_stage(const StepGemv& sg, const ProdDesc* d
   } else {
     for (int i = tid; i < p.K; i += NT) {
       float v = h2f(xsrc[i]);
-      if (add) v = h2f(f2h(v + h2f(p.x2[i])));
+      if (add) v = h2f(f2h(v + h2f(tpj >= 0 ? f2h(tp_sum(sp, tpj, i, rtag)) : p.x2[i])));
       s.xs[i] = f2h(v);
       ss = fmaf(v, v, ss);
     }
@@ -486,7 +561,20 @@ __device__ __forceinline__ void gemv_stage(const StepGemv& sg, const ProdDesc* d
     }
   }
   __syncthreads();
-  gemv_epilogue<NT>(p, s.acc, q.g0, q.ng, RG, cta, ncta);
+  if (sg.tp_send >= 0) {
+    // Row-parallel shard: this CTA's fp32 partial rows go to slot
+    // [tp_send][rank] of every rank's exchange area (over NVLink).
+    const int row_lo = q.g0 * RG;
+    const int nrows = min(q.ng * RG, max(0, p.rows_total - row_lo));
+    const size_t off = ((size_t)sg.tp_send * sp.tp_world + sp.tp_rank) * sp.tp_dim + row_lo;
+    const uint32_t stag = tp_tag(sp, epoch, sg.tp_send);
+    for (int k = tid; k < nrows * sp.tp_world; k += NT) {
+      const int r = k / nrows, v = k - r * nrows;
+      tp_put(sp.tp_vals[r] + off + v, s.acc[v], stag);
+    }
+  } else {
+    gemv_epilogue<NT>(p, s.acc, q.g0, q.ng, RG, cta, ncta);
+  }
   __syncthreads();
 }
 
@@ -730,23 +818,6 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, 
   }
 }
 
-// L2 prefetch of the cached K / V rows this CTA's attention units will read
-// (issued a stage ahead, while HBM streams weights; one thread).
-__device__ __forceinline__ void attn_prefetch_l2(const AttnParams& a, int pos, unsigned cta, unsigned ncta) {
-  if (threadIdx.x != 0 || pos < 0 || pos >= a.S_max) return;
-  const int units = a.Hkv * a.splits, P = pos + 1;
-  for (int u = (int)cta; u < units; u += (int)ncta) {
-    const int split = u % a.splits, kvh = u / a.splits;
-    const int pb = (int)(((int64_t)split * P) / a.splits);
-    const int pe = min((int)(((int64_t)(split + 1) * P) / a.splits), pos);  // row `pos` is written this step
-    if (pe <= pb) continue;
-    const size_t off = ((size_t)kvh * a.S_max + pb) * kAttnD;
-    const uint32_t bytes = (uint32_t)(pe - pb) * kAttnD * 2u;
-    bulk_prefetch_l2(a.k_cache + off, bytes);
-    bulk_prefetch_l2(a.v_cache + off, bytes);
-  }
-}
-
 // ---------------------------------------------------------------------------
 // The persistent kernel (D: ring depth in items per warp).
 // ---------------------------------------------------------------------------
@@ -756,14 +827,14 @@ static_assert(sizeof(StepGemv) % 4 == 0 && sizeof(AttnParams) % 4 == 0, "paramet
 static_assert(kGemvWords <= kStepThreads && kAttnWords <= kStepThreads, "one parameter word per thread");
 
 template <int D>
-__device__ __forceinline__ void run_gemv(const StepGemv& sg, const ProdDesc* descs, int ngemv, unsigned cta,
-                                         unsigned ncta, unsigned char* act, Ring& R, uint64_t* pre_bar,
-                                         unsigned pre_uses) {
+__device__ __forceinline__ void run_gemv(const StepParams& sp, const StepGemv& sg, const ProdDesc* descs, int ngemv,
+                                         unsigned cta, unsigned ncta, unsigned char* act, Ring& R, uint64_t* pre_bar,
+                                         unsigned pre_uses, unsigned long long epoch) {
   switch (sg.lanes) {
-    case 32: gemv_stage<32, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
-    case 16: gemv_stage<16, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
-    case 8: gemv_stage<8, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
-    default: gemv_stage<4, D>(sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses); break;
+    case 32: gemv_stage<32, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
+    case 16: gemv_stage<16, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
+    case 8: gemv_stage<8, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
+    default: gemv_stage<4, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
   }
 }
 
@@ -808,16 +879,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   if (sp.nstages > 0 && s_kind[0] == kStageGemv) gemv_pre_smem(s_g[0], ncta, act, &s_pre_bar, pre_uses);
   __syncthreads();
   int gn = 0, an = 0;  // ordinals of the next GEMV / attention stage
+  const unsigned long long epoch = (sp.tp_world > 1) ? *reinterpret_cast<volatile unsigned long long*>(sp.tp_epoch) : 0ull;
   for (int s = 0; s < sp.nstages; ++s) {
+    int tp_j = -1;            // exchange point this stage feeds (tensor parallel)
+    __half* tp_out = nullptr;
     if (s_kind[s] == kStageGemv) {
       // The next GEMV stage's parameters: loaded now, stored after this
       // stage into the slot GEMV gn-1 used.
       const bool more = gn + 1 < sp.ngemv;
       uint32_t stash = 0u;
       if (more && tid < kGemvWords) stash = __ldg(reinterpret_cast<const uint32_t*>(sp.gemv + gn + 1) + tid);
-      if (s + 1 < sp.nstages && s_kind[s + 1] == kStageAttn && an < sp.nattn)
-        attn_prefetch_l2(s_attn[an & 1], s_pos, cta, ncta);
-      run_gemv<D>(s_g[gn & 1], s_desc, sp.ngemv, cta, ncta, act, R, &s_pre_bar, pre_uses);
+      tp_j = s_g[gn & 1].tp_send;
+      tp_out = s_g[gn & 1].g.out;
+      run_gemv<D>(sp, s_g[gn & 1], s_desc, sp.ngemv, cta, ncta, act, R, &s_pre_bar, pre_uses, epoch);
       if (more && tid < kGemvWords) reinterpret_cast<uint32_t*>(&s_g[(gn + 1) & 1])[tid] = stash;
       ++gn;
     } else {
@@ -836,7 +910,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
     unsigned long long* tr = sp.trace ? sp.trace + 1 + (size_t)s * (ncta + 1) : nullptr;
     if (tr != nullptr && tid == 0) tr[cta] = global_timer_ns();
-    if (s + 1 < sp.nstages) {
+    if (tp_j >= 0) {
+      // Tensor-parallel exchange point: the partial rows went out in the
+      // epilogue and carry their own arrival tags, so no barrier here: the
+      // next stage's prologue waits for exactly the words it adds.  This GPU's
+      // grid arrival s is still counted, keeping later barrier targets.
+      if (s + 1 < sp.nstages) {
+        grid_arrive(sp.bar_count);
+        if (s_kind[s + 1] == kStageGemv) gemv_pre_smem(s_g[gn & 1], ncta, act, &s_pre_bar, pre_uses);
+      } else if (tp_out != nullptr) {
+        // Last stage: the reduced vector is the step's output (read by the
+        // next launch), each CTA writing a slice.
+        const uint32_t tag = tp_tag(sp, epoch, tp_j);
+        const int i0 = (int)(((int64_t)cta * sp.tp_dim) / ncta), i1 = (int)(((int64_t)(cta + 1) * sp.tp_dim) / ncta);
+        for (int i = i0 + tid; i < i1; i += kStepThreads) tp_out[i] = f2h(tp_sum(sp, tp_j, i, tag));
+      }
+      __syncthreads();
+      if (tr != nullptr && cta == 0 && tid == 0) tr[ncta] = global_timer_ns();
+    } else if (s + 1 < sp.nstages) {
       grid_arrive(sp.bar_count);  // includes __syncthreads: the stored parameters are visible
       if (s_kind[s + 1] == kStageGemv) gemv_pre_smem(s_g[gn & 1], ncta, act, &s_pre_bar, pre_uses);
       if (!grid_wait(sp.bar_count, ncta, (unsigned)s)) {
@@ -850,7 +941,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-  step_exit(sp.bar_count, sp.bar_exit, ncta);
+  step_exit(sp.bar_count, sp.bar_exit, ncta, sp.tp_world > 1 ? sp.tp_epoch : nullptr);
   grid_dep_launch_dependents();
 }
 

@@ -9,8 +9,10 @@ weights per GPU:
   intermediate rows); the embedding table and the norms are replicated;
 * the o- and down-projections are split by input columns in whole mask
   groups (M columns), so every shard is itself a shared-mask N:M matrix with
-  the matching rows of ``mat_index``; their fp16 partial outputs are summed by
-  an NCCL all-reduce captured in the step's CUDA graph;
+  the matching rows of ``mat_index``; their partial outputs are summed either
+  inside the persistent step kernel (fp32 partials written into every rank's
+  exchange area over NVLink, summed in rank order) or, with the plan executor,
+  by an NCCL all-reduce of fp16 partials captured in the step's CUDA graph;
 * the output head is split by vocabulary rows; every rank takes the argmax of
   its logits (first index on ties, as ``torch.argmax``), the (value, index)
   candidates are all-gathered, and the global greedy token is the largest
@@ -23,6 +25,7 @@ library.
 """
 from __future__ import annotations
 
+import ctypes
 import dataclasses
 from typing import Optional, Tuple
 
@@ -142,11 +145,84 @@ def gather_candidates(local: torch.Tensor, world: int, group=None) -> torch.Tens
 
 
 class TensorParallel:
-    """Collectives of one rank's decode step (NCCL, captured in the graph)."""
+    """Collectives of one rank's decode step: NCCL (captured in the graph)
+    for the plan executor and the head; with :meth:`enable_persistent` the
+    o-/down-projection all-reduces run inside the persistent step kernel over
+    NVLink peer memory."""
 
     def __init__(self, info: ShardInfo, device: torch.device, group=None):
         self.info, self.group = info, group
+        self.device = device
         self.cand = torch.zeros(2, dtype=torch.float32, device=device)
+        self._own_area = None
+        self._peer_areas = []
+
+    def enable_persistent(self, engine) -> None:
+        """Give ``engine`` a persistent step over its layers whose exchange
+        points (after every o- and down-projection) write partial rows into
+        every rank's exchange area: one cudaMalloc'd area per rank, mapped
+        into the other processes through CUDA IPC handles swapped with an
+        all-gather.  Raises NotImplementedError if the step does not fit."""
+        from . import _lib
+
+        lib = _lib.lib()
+        w, r = self.info.world, self.info.rank
+        recs = list(range(engine._head_index))
+        arr = (ctypes.c_int32 * len(recs))(*recs)
+        step = ctypes.c_void_p()
+        _lib.check(lib.nms_step_create(engine._plan, arr, len(recs), ctypes.byref(step)), "nms_step_create")
+        try:
+            nreduce, dim = len(engine.cut_points), engine.config.dim
+            nbytes = lib.nms_tp_area_bytes(nreduce, w, dim)
+            own = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(64)
+            with torch.cuda.device(self.device):
+                _lib.check(lib.nms_ipc_alloc(nbytes, ctypes.byref(own), handle), "nms_ipc_alloc")
+            self._own_area = own
+            handles = [None] * w
+            dist.all_gather_object(handles, handle.raw, group=self.group)
+            areas = []
+            for k in range(w):
+                if k == r:
+                    areas.append(own.value)
+                    continue
+                p = ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    _lib.check(lib.nms_ipc_open(ctypes.create_string_buffer(handles[k], 64), ctypes.byref(p)),
+                               "nms_ipc_open")
+                self._peer_areas.append(p)
+                areas.append(p.value)
+            cfg = _lib.NmsTpConfig()
+            cfg.world, cfg.rank, cfg.dim = w, r, dim
+            for k, a in enumerate(areas):
+                cfg.area[k] = a
+            stages = [c - 1 for c in engine.cut_points]
+            sarr = (ctypes.c_int32 * len(stages))(*stages)
+            _lib.check(lib.nms_step_set_tp(step, sarr, len(stages), ctypes.byref(cfg)), "nms_step_set_tp")
+        except Exception:
+            lib.nms_step_destroy(step)
+            self.close()
+            raise
+        engine._steps["tp"] = step
+        engine.mode = "persistent_tp"
+
+    def close(self) -> None:
+        """Unmap the peers' exchange areas and free this rank's (after every
+        rank is done with them)."""
+        from . import _lib
+
+        if self._own_area is None and not self._peer_areas:
+            return
+        lib = _lib.lib()
+        torch.cuda.synchronize(self.device)
+        if dist.is_initialized():
+            dist.barrier(group=self.group)
+        for p in self._peer_areas:
+            lib.nms_ipc_close(p)
+        self._peer_areas = []
+        if self._own_area is not None:
+            lib.nms_ipc_free(self._own_area)
+            self._own_area = None
 
     def allreduce(self, t: torch.Tensor) -> None:
         dist.all_reduce(t, group=self.group)
@@ -170,9 +246,12 @@ class TensorParallel:
 
 def build_tp_engine(cfg, nm: Optional[Tuple[int, int]], world: int, rank: int, device: torch.device, *,
                     max_seq: int, seed: int = 0, prefetch_bytes: int = 0, next_prefetch_bytes: int = 0,
-                    history_len: int = 0, group=None):
+                    history_len: int = 0, group=None, mode: str = "auto"):
     """This rank's decode engine for ``cfg`` (the same weights as the
-    single-GPU model built with ``seed``), and its TensorParallel state."""
+    single-GPU model built with ``seed``), and its TensorParallel state.
+    ``mode``: "plan" (NCCL all-reduces between launches), "persistent"
+    (all-reduces inside the persistent step over NVLink) or "auto"
+    (persistent when it fits)."""
     from .engine import DecodeEngine
     from .generate import build_model
 
@@ -183,4 +262,10 @@ def build_tp_engine(cfg, nm: Optional[Tuple[int, int]], world: int, rank: int, d
     eng = DecodeEngine(model, max_seq, prefetch_bytes=prefetch_bytes, next_prefetch_bytes=next_prefetch_bytes,
                        history_len=history_len, mode="plan", allreduce=tp.allreduce, tp_rank=rank, tp_size=world,
                        local_heads=info.local_heads, head_hook=lambda adv: tp.head_hook(eng, adv))
+    if mode in ("auto", "persistent"):
+        try:
+            tp.enable_persistent(eng)
+        except NotImplementedError:
+            if mode == "persistent":
+                raise
     return eng, tp
