@@ -68,6 +68,15 @@ int nms_device_error(int* code_out, int clear);
 int nms_gemv_f16(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K,
                  int64_t w, int64_t h, int32_t block_width, int32_t vec_width, void* stream);
 
+/* Per-row N:M on the reference layout: the non-shared index layout of
+ * src/spmv/nmsparse_linear.py:27-29 (mat_index u8 [w, h], element (j, r) at
+ * j*h + r, each row with its own in-group offsets; the reference ships no
+ * kernel for it, src/spmv/nmsparse_op.py:33-44,98-116):
+ *   out[r] = sum_j mat_data[j, r] * vec[(j/N)*M + mat_index[j, r]]
+ * Same shape rules as nms_gemv_f16; mat_index 16-byte aligned; K <= ~110k. */
+int nms_gemv_rowwise_f16(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K,
+                         int64_t w, int64_t h, int32_t block_width, int32_t vec_width, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Packed layout (the re-laid-out packer; no reference counterpart: the
  * reference streams mat_data[w, h] directly, triton_spmv.py:100-106).

@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "nms_num_sms",
     "nms_device_error",
     "nms_gemv_f16",
+    "nms_gemv_rowwise_f16",
     "nms_packed_row_stride",
     "nms_pack_f16",
     "nms_unpack_f16",
@@ -162,6 +163,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "nms_num_sms": (I32, [ctypes.POINTER(I32)]),
         "nms_device_error": (I32, [ctypes.POINTER(I32), I32]),
         "nms_gemv_f16": (I32, [P, P, P, P, I64, I64, I64, I32, I32, P]),
+        "nms_gemv_rowwise_f16": (I32, [P, P, P, P, I64, I64, I64, I32, I32, P]),
         "nms_packed_row_stride": (I64, [I64]),
         "nms_pack_f16": (I32, [P, P, I64, I64, I64, P]),
         "nms_unpack_f16": (I32, [P, P, I64, I64, I64, P]),

@@ -578,15 +578,43 @@ struct GemvRefParams {
   int32_t cs;      // cluster size (1 = no cluster)
 };
 
-template <int LR>
+__device__ __forceinline__ uint4 ld_stream_128(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// One weight element (row = lane's 16 rows, e) of a per-row layout: the
+// gathered input is x[(j / N) * M + index byte e].
+__device__ __forceinline__ void fma_rowwise16(float (&acc)[16], const U32x8& wv, const uint4& iv, const __half* xs,
+                                              int gbase) {
+  const uint8_t* ib = reinterpret_cast<const uint8_t*>(&iv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 wf = __half22float2(*reinterpret_cast<const __half2*>(&wv.v[e]));
+    acc[2 * e] = fmaf(wf.x, h2f(xs[gbase + ib[2 * e]]), acc[2 * e]);
+    acc[2 * e + 1] = fmaf(wf.y, h2f(xs[gbase + ib[2 * e + 1]]), acc[2 * e + 1]);
+  }
+}
+
+// Reference layout [w, h]: lanes own 16 consecutive rows, warps and cluster
+// ranks split the compressed width j.  ROW = false: shared mask
+// (mat_index [w/N, N]), the gathered vector xc[j] is built once per CTA.
+// ROW = true: per-row mask (mat_index [w, h], the reference's non-shared
+// layout, src/spmv/nmsparse_linear.py:27-29): the full input vector is staged
+// and every element gathers its own column.
+template <int LR, bool ROW>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_ref_kernel(const __grid_constant__ GemvRefParams p) {
   constexpr int RB = 16 * LR;
   constexpr int JPW = kWarp / LR;           // j rows per warp instruction
   constexpr int JL = kGemvWarps * JPW;      // j lanes per CTA
   constexpr int U = 4;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __half* xc = reinterpret_cast<__half*>(smem_raw);  // [jchunk]
-  float* red = reinterpret_cast<float*>(smem_raw + align_up_sz((size_t)p.jchunk * 2, 16));  // [kGemvWarps][RB]
+  __half* xc = reinterpret_cast<__half*>(smem_raw);  // [jchunk] (ROW: [K + 256], zero tail)
+  const size_t xbytes = align_up_sz((size_t)(ROW ? p.K + 256 : p.jchunk) * 2, 16);
+  float* red = reinterpret_cast<float*>(smem_raw + xbytes);  // [kGemvWarps][RB]
   float* part = red + kGemvWarps * RB;  // [RB]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -596,9 +624,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_ref_kernel(const __grid_
   const int j1 = min(p.w, j0 + p.jchunk);
 
   grid_dep_wait();
-  for (int j = j0 + tid; j < j1; j += kGemvThreads) {
-    const int col = (j / p.n) * p.m + (int)p.mat_index[j];
-    xc[j - j0] = (col < p.K) ? p.vec[col] : __ushort_as_half((unsigned short)0);
+  if (ROW) {
+    // An index byte is at most 255 past its group start: the zero tail keeps
+    // every gather inside shared memory whatever the mask holds.
+    for (int k = tid; k < p.K + 256; k += kGemvThreads) xc[k] = k < p.K ? p.vec[k] : __ushort_as_half((unsigned short)0);
+  } else {
+    for (int j = j0 + tid; j < j1; j += kGemvThreads) {
+      const int col = (j / p.n) * p.m + (int)p.mat_index[j];
+      xc[j - j0] = (col < p.K) ? p.vec[col] : __ushort_as_half((unsigned short)0);
+    }
   }
   __syncthreads();
   grid_dep_launch_dependents();
@@ -612,36 +646,50 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_ref_kernel(const __grid_
   for (int k = 0; k < 16; ++k) acc[k] = 0.f;
 
   const __half* base = p.mat_data + row0;
+  const uint8_t* ibase = p.mat_index + row0;  // ROW: index bytes of the lane's rows
   int j = j0 + q;
   for (; j + (U - 1) * JL < j1; j += U * JL) {
     U32x8 r[U];
+    uint4 ix[ROW ? U : 1];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (row_ok) {
         r[u] = ld_stream_256(base + (size_t)(j + u * JL) * p.h);
+        if (ROW) ix[u] = ld_stream_128(ibase + (size_t)(j + u * JL) * p.h);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) r[u].v[e] = 0u;
+        if (ROW) ix[u] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const uint16_t xh = __half_as_ushort(xc[j + u * JL - j0]);
+      if (ROW) {
+        fma_rowwise16(acc, r[u], ix[u], xc, ((j + u * JL) / p.n) * p.m);
+      } else {
+        const uint16_t xh = __half_as_ushort(xc[j + u * JL - j0]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) fma2_f32_f16_bcast(acc[2 * e], acc[2 * e + 1], r[u].v[e], xh);
+        for (int e = 0; e < 8; ++e) fma2_f32_f16_bcast(acc[2 * e], acc[2 * e + 1], r[u].v[e], xh);
+      }
     }
   }
   for (; j < j1; j += JL) {
     U32x8 r;
+    uint4 ix = make_uint4(0u, 0u, 0u, 0u);
     if (row_ok) {
       r = ld_stream_256(base + (size_t)j * p.h);
+      if (ROW) ix = ld_stream_128(ibase + (size_t)j * p.h);
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) r.v[e] = 0u;
     }
-    const uint16_t xh = __half_as_ushort(xc[j - j0]);
+    if (ROW) {
+      fma_rowwise16(acc, r, ix, xc, (j / p.n) * p.m);
+    } else {
+      const uint16_t xh = __half_as_ushort(xc[j - j0]);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) fma2_f32_f16_bcast(acc[2 * e], acc[2 * e + 1], r.v[e], xh);
+      for (int e = 0; e < 8; ++e) fma2_f32_f16_bcast(acc[2 * e], acc[2 * e + 1], r.v[e], xh);
+    }
   }
 
   // Reduce across the JPW j-subgroups of the warp.

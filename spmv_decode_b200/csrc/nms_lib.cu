@@ -85,7 +85,7 @@ int device_info(const DeviceInfo** out) {
     const void* dyn_smem_kernels[] = {
         (const void*)nms::gemv_packed_kernel<32>, (const void*)nms::gemv_packed_kernel<16>,
         (const void*)nms::gemv_packed_kernel<8>,  (const void*)nms::gemv_packed_kernel<4>,
-        (const void*)nms::gemv_ref_kernel<8>,
+        (const void*)nms::gemv_ref_kernel<8, false>, (const void*)nms::gemv_ref_kernel<8, true>,
     };
     size_t static_max = 0;
     for (const void* k : dyn_smem_kernels) {
@@ -167,6 +167,7 @@ struct EmbedParams {
 struct LaunchRec {
   enum Kind { kGemvPacked, kGemvRef, kAttention, kEmbedding, kPack, kUnpack } kind;
   int lanes = 0;  // gemv_packed_kernel template argument
+  bool rowwise = false;  // kGemvRef: per-row mask (mat_index [w, h])
   int amax_capacity = 0;  // argmax epilogue: partials the caller's scratch holds
   nms::GemvParams gp;
   nms::GemvRefParams rp;
@@ -194,7 +195,8 @@ int launch_rec(const LaunchRec& r, cudaStream_t st) {
       }
       break;
     case LaunchRec::kGemvRef:
-      e = launch_ex(nms::gemv_ref_kernel<8>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.rp);
+      e = r.rowwise ? launch_ex(nms::gemv_ref_kernel<8, true>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.rp)
+                    : launch_ex(nms::gemv_ref_kernel<8, false>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.rp);
       break;
     case LaunchRec::kAttention:
       e = launch_ex(nms::attention_decode_kernel, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.ap);
@@ -533,14 +535,15 @@ int nms_device_error(int* code_out, int clear) {
   return NMS_OK;
 }
 
-int nms_gemv_f16(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K, int64_t w,
-                 int64_t h, int32_t block_width, int32_t vec_width, void* stream) {
+static int gemv_ref_launch(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K,
+                           int64_t w, int64_t h, int32_t block_width, int32_t vec_width, void* stream, bool rowwise) {
   if (!vec || !mat_data || !mat_index || !out) return fail(NMS_ERR_VALUE, "null pointer argument");
   int rc = check_nm(K, w, block_width, vec_width);
   if (rc) return rc;
   if (h <= 0 || h % 128 != 0) return fail(NMS_ERR_VALUE, "h must be divisible by 128 (got %lld)", (long long)h);
   if (h > (1 << 28)) return fail(NMS_ERR_VALUE, "h=%lld too large", (long long)h);
   if (!aligned(mat_data, 32)) return fail(NMS_ERR_VALUE, "mat_data must be 32-byte aligned");
+  if (rowwise && !aligned(mat_index, 16)) return fail(NMS_ERR_VALUE, "per-row mat_index must be 16-byte aligned");
   const DeviceInfo* dev = nullptr;
   rc = device_info(&dev);
   if (rc) return rc;
@@ -566,13 +569,24 @@ int nms_gemv_f16(const void* vec, const void* mat_data, const void* mat_index, v
   p.jchunk = (int32_t)jchunk;
   p.cs = cs;
   rec.kind = LaunchRec::kGemvRef;
-  rec.smem = nms::align_up_sz((size_t)jchunk * 2, 16) + (size_t)(nms::kGemvWarps + 1) * RB * 4;
+  rec.rowwise = rowwise;
+  rec.smem = nms::align_up_sz((size_t)(rowwise ? K + 256 : jchunk) * 2, 16) + (size_t)(nms::kGemvWarps + 1) * RB * 4;
   if (rec.smem > dev->max_smem_optin)
-    return fail(NMS_ERR_NOT_IMPLEMENTED, "w=%lld too large for one CTA slice", (long long)w);
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "%s too large for one CTA slice", rowwise ? "K" : "w");
   rec.grid = dim3((unsigned)nblocks, (unsigned)cs);
   rec.block = dim3(nms::kGemvThreads);
   rec.cluster = dim3(1, (unsigned)cs, 1);
   return launch_rec(rec, static_cast<cudaStream_t>(stream));
+}
+
+int nms_gemv_f16(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K, int64_t w,
+                 int64_t h, int32_t block_width, int32_t vec_width, void* stream) {
+  return gemv_ref_launch(vec, mat_data, mat_index, out, K, w, h, block_width, vec_width, stream, false);
+}
+
+int nms_gemv_rowwise_f16(const void* vec, const void* mat_data, const void* mat_index, void* out, int64_t K,
+                         int64_t w, int64_t h, int32_t block_width, int32_t vec_width, void* stream) {
+  return gemv_ref_launch(vec, mat_data, mat_index, out, K, w, h, block_width, vec_width, stream, true);
 }
 
 int64_t nms_packed_row_stride(int64_t w) {

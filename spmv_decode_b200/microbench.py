@@ -17,6 +17,8 @@ For every shape (out x in) and N:M ratio: seeded synthetic shared-mask weights
                   (the kernel behind ``nmsparse::gemv``);
 * ``cublas``   -- dense fp16 ``torch.mv`` (cuBLAS) on a dense matrix of the
                   same shape (the control);
+* ``rowwise``  -- the per-row layout (top-|w| per row and
+                  group, one uint8 offset per kept value) at 32:64;
 
 each as a CUDA graph of back-to-back launches over enough weight copies to
 span more than 3x the 126 MB L2 (so every launch streams from HBM), timed with
@@ -184,6 +186,41 @@ def bench_shape(h: int, K: int, ratios, dev, reps: int, peak: float) -> list:
     return rows
 
 
+def bench_rowwise(h: int, K: int, n: int, m: int, dev, reps: int, peak: float) -> dict:
+    """Per-row N:M (BASELINE config 1 layout: values [w, h] + one uint8 offset
+    per value) through nms_gemv_rowwise_f16; top-|w| packing of N(0, 0.02)."""
+    from .nmsparse_linear import make_rowwise_topk
+
+    lib = _lib.lib()
+    w = K // m * n
+    alg = h * w * 2 + h * w + K * 2 + h * 2
+    nb = max(2, math.ceil(3 * L2_BYTES / alg) + 1)
+    g = torch.Generator(device=dev).manual_seed(0)
+    W0 = (torch.randn(h, K, device=dev, generator=g) * 0.02).to(torch.float16)
+    md, mi = make_rowwise_topk(W0, n, m)
+    del W0
+    mats = [(md.clone(), mi.clone()) for _ in range(nb)]
+    x = torch.randn(K, device=dev).to(torch.float16)
+    outs = [torch.empty(h, device=dev, dtype=torch.float16) for _ in range(nb)]
+
+    def fn(i):
+        a, b = mats[i]
+        return lambda s: _lib.check(lib.nms_gemv_rowwise_f16(x.data_ptr(), a.data_ptr(), b.data_ptr(),
+                                                             outs[i].data_ptr(), K, w, h, n, m, s.cuda_stream),
+                                    "nms_gemv_rowwise_f16")
+
+    t = _graph_time_us([fn(i) for i in range(nb)], dev, reps)
+    cols = (torch.arange(w, device=dev) // n)[:, None] * m + mi.long()
+    ref = (md.float() * x.float()[cols]).sum(0)
+    r = {"shape": f"{h}x{K}", "nm": f"{n}:{m} per-row", "algorithmic_bytes": alg,
+         "rowwise_us": round(t, 3), "rowwise_GBs": round(alg / t / 1e3, 1), "rowwise_frac": round(alg / t / 1e3 / peak, 3),
+         "rowwise_max_rel": _max_rel(outs[0], ref)}
+    print(json.dumps(r), flush=True)
+    del mats, outs
+    torch.cuda.empty_cache()
+    return r
+
+
 def bench_dense_head(dev, reps: int, peak: float, V: int = 128256, K: int = 4096) -> dict:
     """The dense lm_head shape: cuBLAS torch.mv against this library's dense
     GEMV (the head launch of the decode step, without its argmax)."""
@@ -218,6 +255,7 @@ def main(argv=None):
     p.add_argument("--ratios", default=",".join(f"{n}:{m}" for n, m in RATIOS))
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--no-head", action="store_true")
+    p.add_argument("--no-rowwise", action="store_true")
     args = p.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
     peak, src = _peak_gbs()
@@ -226,6 +264,9 @@ def main(argv=None):
     rows = []
     for h, K in shapes:
         rows += bench_shape(h, K, ratios, dev, args.reps, peak)
+    if not args.no_rowwise:
+        for h, K in shapes:
+            rows.append(bench_rowwise(h, K, 32, 64, dev, args.reps, peak))
     if not args.no_head:
         rows.append(bench_dense_head(dev, args.reps, peak))
     print(json.dumps({"summary": True, "peak_GBs": peak, "peak_source": src, "rows": len(rows)}), flush=True)

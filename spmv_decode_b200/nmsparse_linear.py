@@ -97,6 +97,26 @@ def masked_dense(mat_data: torch.Tensor, mat_index: torch.Tensor, K: int, M: int
     return dense
 
 
+def make_rowwise_topk(weight: torch.Tensor, n: int, m: int):
+    """Per-row top-|w| N:M packing of a dense [h, K] weight:
+    for every row and group of m consecutive input columns keep the n largest
+    |w| (ties go to the lower column), offsets ascending within the group.
+    Returns (mat_data [w, h] fp16, mat_index [w, h] uint8) in the reference's
+    per-row layout (src/spmv/nmsparse_linear.py:27-29), on weight's device."""
+    h, K = weight.shape
+    if K % m or n <= 0 or n > m or m > 256:
+        raise ValueError(f"K={K} must be a multiple of M={m}, 0 < N <= M <= 256")
+    G = K // m
+    Wg = weight.to(torch.float16).reshape(h, G, m)
+    # Stable descending sort keeps the lower column first among equal |w|.
+    order = torch.sort(Wg.float().abs(), dim=2, descending=True, stable=True).indices[:, :, :n]
+    off = torch.sort(order, dim=2).values
+    vals = torch.gather(Wg, 2, off)
+    mat_data = vals.reshape(h, G * n).t().contiguous()
+    mat_index = off.reshape(h, G * n).t().contiguous().to(torch.uint8)
+    return mat_data, mat_index
+
+
 class NmSparseLinear(nn.Module):
     """Shared-mask 50% N:M sparse linear (reference: src/spmv/nmsparse_linear.py:36-68)."""
 

@@ -56,9 +56,12 @@ def _validate_forward(vec: torch.Tensor, mat_data: torch.Tensor, mat_index: torc
     num_groups = w // block_width
     if tuple(mat_data.shape) != (w, h):
         raise ValueError(f"mat_data must have shape {(w, h)}, got {tuple(mat_data.shape)}")
-    if tuple(mat_index.shape) != (num_groups, block_width):
+    # Shared mask [G, N]; or the per-row layout [w, h] (one offset per kept
+    # value, src/spmv/nmsparse_linear.py:27-29).
+    if tuple(mat_index.shape) not in ((num_groups, block_width), (w, h)):
         raise ValueError(
-            f"mat_index must have shape {(num_groups, block_width)}, got {tuple(mat_index.shape)}"
+            f"mat_index must have shape {(num_groups, block_width)} (shared mask) or {(w, h)} (per-row), "
+            f"got {tuple(mat_index.shape)}"
         )
     if not mat_data.is_contiguous():
         raise ValueError("mat_data must be contiguous")
@@ -81,13 +84,15 @@ def nmsparse_spmv_forward(vec: torch.Tensor, mat_data: torch.Tensor, mat_index: 
     if vec.dtype != torch.float16:
         raise TypeError("the sm_100a kernel computes fp16 x fp16 -> fp32; cast inputs to float16")
     out = torch.empty((1, h), dtype=torch.float16, device=vec.device)
+    rowwise = tuple(mat_index.shape) == (w, h) and (w, h) != (w // block_width, block_width)
+    fn = "nms_gemv_rowwise_f16" if rowwise else "nms_gemv_f16"
     with torch.cuda.device(vec.device):
         _lib.check(
-            _lib.lib().nms_gemv_f16(
+            getattr(_lib.lib(), fn)(
                 vec.data_ptr(), mat_data.data_ptr(), mat_index.data_ptr(), out.data_ptr(),
                 int(K), int(w), int(h), int(block_width), int(vec_width), _stream_ptr(vec.device),
             ),
-            "nms_gemv_f16",
+            fn,
         )
     return out
 
@@ -95,7 +100,8 @@ def nmsparse_spmv_forward(vec: torch.Tensor, mat_data: torch.Tensor, mat_index: 
 @torch.library.custom_op("nmsparse::gemv", mutates_args=())
 def gemv(x: torch.Tensor, mat_data: torch.Tensor, mat_index: torch.Tensor,
          w: int, h: int, block_width: int, vec_width: int) -> torch.Tensor:
-    """Shared-mask N:M GEMV, reference layout (src/spmv/nmsparse_op.py:77-96)."""
+    """N:M GEMV on the reference layout (src/spmv/nmsparse_op.py:77-96):
+    shared mask (mat_index [w/N, N]) or per-row mask (mat_index [w, h])."""
     K = x.shape[-1]
     x2d = x.reshape(-1, K).contiguous()
     if x2d.shape[0] != 1:
