@@ -244,6 +244,8 @@ def main():
     if world > 1:
         from datetime import timedelta
 
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "WARN"  # no version banner: stdout carries the one JSON line
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     nm = None if args.nm == "dense" else tuple(int(v) for v in args.nm.split(":"))
     cfg = model_config(args)
@@ -273,7 +275,7 @@ def main():
     assert torch.isfinite(eng.logits.float()).all(), "non-finite logits after replay"
     # Kernels of this library per step: one persistent kernel, or the plan's
     # launches (the plan holds the head twice: fixed and advancing variants).
-    launches_per_step = {"persistent": 1, "persistent_tp": 2}.get(eng.mode, eng.size() - 1)
+    launches_per_step = {"persistent": 1, "persistent_tp": 1}.get(eng.mode, eng.size() - 1)
     engine_mode = eng.mode
     dev_err = _lib.device_error()
 
@@ -341,7 +343,7 @@ def main():
     # replay time; with the plan executor the GEMV kernel above dominates.
     if engine_mode in ("persistent", "persistent_tp"):
         step_achieved = sb["total"] / (ms * 1e-3) / 1e9
-        kname = "decode_step_kernel" if engine_mode == "persistent" else "decode_step_kernel (+ head GEMV, NCCL argmax)"
+        kname = "decode_step_kernel"
         roofline = {"bound": "hbm", "kernel": kname, "achieved": round(step_achieved, 1),
                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(step_achieved / peaks["hbm_gbs"], 4),
                     "peak_source": peaks["source"],

@@ -291,14 +291,18 @@ int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity);
  * their own arrival signal; the next GEMV stage adds the ranks' partials
  * (rank order, identical on every rank) in place of its residual addend;
  * after a final exchange point the reduced vector is also written to that
- * stage's output.  Waits are bounded (device error 3).  Area layout: step
- * counter (8 bytes, padded to 256) + nreduce x world x dim {fp32, u32 tag}.
+ * stage's output.  If the step ends with a vocabulary-parallel argmax head
+ * (NMS_EPI_ARGMAX), the ranks swap their best (logit, global index) the same
+ * way and every rank writes the global greedy token (largest logit, lowest
+ * index on ties) and runs the head's generation hooks.  Waits are bounded
+ * (device error 3).  Area layout: step counter (8 bytes, padded to 256) +
+ * (nreduce + 1) x world x dim {fp32, u32 tag}.
  * ------------------------------------------------------------------------- */
 #define NMS_MAX_TP 8
 typedef struct nms_tp_config {
   int32_t world, rank;
   int32_t dim;                   /* length of every reduced vector */
-  int32_t pad_;
+  int32_t vocab_offset;          /* first vocabulary row of this rank's head shard */
   void* area[NMS_MAX_TP];        /* every rank's exchange area, as mapped in this process */
 } nms_tp_config;
 

@@ -77,7 +77,7 @@ class NmsTpConfig(ctypes.Structure):
     """nms_tp_config (include/nmsparse_b200.h)."""
 
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("dim", ctypes.c_int32),
-                ("pad_", ctypes.c_int32), ("area", ctypes.c_void_p * NMS_MAX_TP)]
+                ("vocab_offset", ctypes.c_int32), ("area", ctypes.c_void_p * NMS_MAX_TP)]
 
 
 c_void_p = ctypes.c_void_p

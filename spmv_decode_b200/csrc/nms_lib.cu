@@ -904,7 +904,7 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
 
 int64_t nms_tp_area_bytes(int32_t nreduce, int32_t world, int32_t dim) {
   if (nreduce < 1 || world < 1 || dim < 1) return -1;
-  return 256 + (int64_t)nreduce * world * dim * 8;
+  return 256 + (int64_t)(nreduce + 1) * world * (dim < 2 ? 2 : dim) * 8;  // + the head's candidate point
 }
 
 int nms_ipc_alloc(int64_t bytes, void** ptr_out, void* handle_out) {
@@ -948,7 +948,8 @@ int nms_step_set_tp(nms_step* step, const int32_t* reduce_stages, int32_t nreduc
   if (step == nullptr || reduce_stages == nullptr || cfg == nullptr) return fail(NMS_ERR_VALUE, "null argument");
   if (cfg->world < 2 || cfg->world > NMS_MAX_TP || cfg->rank < 0 || cfg->rank >= cfg->world)
     return fail(NMS_ERR_VALUE, "world=%d rank=%d (2 <= world <= %d)", cfg->world, cfg->rank, NMS_MAX_TP);
-  if (nreduce < 1 || cfg->dim < 1) return fail(NMS_ERR_VALUE, "nreduce=%d dim=%d", nreduce, cfg->dim);
+  if (nreduce < 1 || cfg->dim < 2) return fail(NMS_ERR_VALUE, "nreduce=%d dim=%d", nreduce, cfg->dim);
+  if (step->params.tp_world > 1) return fail(NMS_ERR_VALUE, "tensor parallelism is already set for this step");
   for (int r = 0; r < cfg->world; ++r)
     if (cfg->area[r] == nullptr || !aligned(cfg->area[r], 256)) return fail(NMS_ERR_VALUE, "area %d missing or unaligned", r);
   std::vector<nms::StepGemv> g = step->gemvs;
@@ -975,6 +976,23 @@ int nms_step_set_tp(nms_step* step, const int32_t* reduce_stages, int32_t nreduc
       break;
     }
   }
+  // A vocabulary-parallel argmax head as the last stage: the local winner
+  // goes to a scratch word and the kernel's tail swaps candidates.
+  const int last_g = step->gemv_of_stage[step->nstages - 1];
+  const bool head = last_g >= 0 && g[last_g].g.epilogue == nms::kEpiArgmax;
+  if (head) {
+    nms::GemvParams& hp = g[last_g].g;
+    step->params.tp_token_out = hp.token_out;
+    step->params.tp_next_token = hp.next_token;
+    step->params.tp_history = hp.token_history;
+    step->params.tp_pos = hp.pos;
+    step->params.tp_history_len = hp.history_len;
+    step->params.tp_local_best = reinterpret_cast<int64_t*>(reinterpret_cast<unsigned char*>(step->params.bar_count) + 192);
+    hp.token_out = step->params.tp_local_best;
+    hp.next_token = nullptr;
+    hp.token_history = nullptr;
+    hp.pos = nullptr;
+  }
   const size_t cbytes = 256;  // the step counter, then the values
   nms::StepParams& P = step->params;
   cudaError_t e = cudaSetDevice(step->device);
@@ -984,6 +1002,8 @@ int nms_step_set_tp(nms_step* step, const int32_t* reduce_stages, int32_t nreduc
   if (e != cudaSuccess) return fail_cuda(e, "tensor-parallel stage table");
   P.tp_world = cfg->world;
   P.tp_rank = cfg->rank;
+  P.tp_head = head ? 1 : 0;
+  P.tp_vocab_offset = cfg->vocab_offset;
   P.tp_dim = cfg->dim;
   P.tp_nreduce = nreduce;
   for (int r = 0; r < nms::kMaxTp; ++r) {

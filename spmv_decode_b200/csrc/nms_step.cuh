@@ -65,6 +65,15 @@ struct StepParams {
   uint2* tp_vals[kMaxTp];
   const uint2* tp_my_vals;
   unsigned long long* tp_epoch;
+  // Vocabulary-parallel head (last stage, argmax): the local winner goes to
+  // tp_local_best; the global token and the generation hooks are written here.
+  int32_t tp_head, tp_vocab_offset;
+  int64_t* tp_local_best;
+  int64_t* tp_token_out;
+  int64_t* tp_next_token;
+  int64_t* tp_history;
+  int64_t* tp_pos;
+  int64_t tp_history_len;
 };
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -818,6 +827,42 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, 
   }
 }
 
+// Vocabulary-parallel greedy token (one thread, after this GPU's head stage):
+// the rank's (logit, global index) candidate goes to point `nreduce` of every
+// rank's area; the largest logit wins, the lowest index on ties -- the token
+// argmax over the full logits gives.  Then the head's generation hooks.
+__device__ __forceinline__ void tp_head_token(const StepParams& sp, const __half* logits, unsigned long long epoch) {
+  const int64_t li = *reinterpret_cast<volatile int64_t*>(sp.tp_local_best);
+  const float lv = h2f(logits[li]);
+  const uint32_t tag = tp_tag(sp, epoch, sp.tp_nreduce);
+  const size_t slot = ((size_t)sp.tp_nreduce * sp.tp_world + sp.tp_rank) * sp.tp_dim;
+  for (int r = 0; r < sp.tp_world; ++r) {
+    tp_put(sp.tp_vals[r] + slot, lv, tag);
+    tp_put(sp.tp_vals[r] + slot + 1, __uint_as_float((uint32_t)(li + sp.tp_vocab_offset)), tag);
+  }
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  for (int r = 0; r < sp.tp_world; ++r) {
+    const uint2* c = sp.tp_my_vals + ((size_t)sp.tp_nreduce * sp.tp_world + r) * sp.tp_dim;
+    uint2 wv = tp_get(c), wi = tp_get(c + 1);
+    if (wv.y != tag) wv = tp_poll(c, tag);
+    if (wi.y != tag) wi = tp_poll(c + 1, tag);
+    const float v = __uint_as_float(wv.x);
+    if (v > bv || (v == bv && wi.x < bi)) {
+      bv = v;
+      bi = wi.x;
+    }
+  }
+  const int64_t tok = (int64_t)bi;
+  *sp.tp_token_out = tok;
+  if (sp.tp_next_token != nullptr) *sp.tp_next_token = tok;
+  if (sp.tp_pos != nullptr) {
+    const int64_t cur = *sp.tp_pos;
+    if (sp.tp_history != nullptr && cur >= 0 && cur < sp.tp_history_len) sp.tp_history[cur] = tok;
+    *sp.tp_pos = cur + 1;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // The persistent kernel (D: ring depth in items per warp).
 // ---------------------------------------------------------------------------
@@ -939,6 +984,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       }
       if (tr != nullptr && cta == 0 && tid == 0) tr[ncta] = global_timer_ns();
     }
+  }
+  if (sp.tp_world > 1 && sp.tp_head) {
+    // The head's last CTA wrote this rank's winner; every CTA has written its
+    // logits: one grid barrier, then CTA 0 swaps candidates with the peers.
+    grid_arrive(sp.bar_count);
+    if (grid_wait(sp.bar_count, ncta, (unsigned)sp.nstages - 1u) && cta == 0 && tid == 0)
+      tp_head_token(sp, s_g[(gn - 1) & 1].g.out, epoch);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   step_exit(sp.bar_count, sp.bar_exit, ncta, sp.tp_world > 1 ? sp.tp_epoch : nullptr);

@@ -327,12 +327,9 @@ class DecodeEngine:
             _lib.check(_lib.lib().nms_step_launch(self._steps[advance], stream.cuda_stream), "nms_step_launch")
             return
         if self.mode == "persistent_tp":
-            # Layers in one persistent launch with the all-reduces inside it
-            # (tp.TensorParallel.enable_persistent), then the vocab-parallel head.
-            _lib.check(_lib.lib().nms_step_launch(self._steps["tp"], stream.cuda_stream), "nms_step_launch")
-            self._launch(self._head_index, self._head_index + 1, stream)
-            with torch.cuda.stream(stream):
-                self.head_hook(advance)
+            # One persistent launch: the all-reduces and the vocabulary-
+            # parallel greedy token run inside it (tp.TensorParallel.enable_persistent).
+            _lib.check(_lib.lib().nms_step_launch(self._steps[advance], stream.cuda_stream), "nms_step_launch")
             return
         begin = 0
         if self.allreduce is not None:
@@ -392,7 +389,7 @@ class DecodeEngine:
         if self.mode not in ("persistent", "persistent_tp"):
             raise RuntimeError("the timeline needs the persistent executor")
         L = _lib.lib()
-        h = self._steps["tp" if self.mode == "persistent_tp" else advance]
+        h = self._steps[advance]
         ns, grid = ctypes.c_int32(), ctypes.c_int32()
         _lib.check(L.nms_step_info(h, ctypes.byref(ns), ctypes.byref(grid)))
         n, g = int(ns.value), int(grid.value)

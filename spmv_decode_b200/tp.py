@@ -158,20 +158,25 @@ class TensorParallel:
         self._peer_areas = []
 
     def enable_persistent(self, engine) -> None:
-        """Give ``engine`` a persistent step over its layers whose exchange
-        points (after every o- and down-projection) write partial rows into
-        every rank's exchange area: one cudaMalloc'd area per rank, mapped
-        into the other processes through CUDA IPC handles swapped with an
-        all-gather.  Raises NotImplementedError if the step does not fit."""
+        """Give ``engine`` persistent steps (fixed and advancing) over all its
+        stages: exchange points after every o- and down-projection write
+        partial rows into every rank's exchange area, and the vocabulary-
+        parallel head swaps its (logit, index) candidates the same way.  One
+        cudaMalloc'd area per rank, mapped into the other processes through
+        CUDA IPC handles swapped with an all-gather.  Raises
+        NotImplementedError if the step does not fit."""
         from . import _lib
 
         lib = _lib.lib()
         w, r = self.info.world, self.info.rank
-        recs = list(range(engine._head_index))
-        arr = (ctypes.c_int32 * len(recs))(*recs)
-        step = ctypes.c_void_p()
-        _lib.check(lib.nms_step_create(engine._plan, arr, len(recs), ctypes.byref(step)), "nms_step_create")
+        steps = {}
         try:
+            for adv in (False, True):
+                recs = list(range(engine._head_index)) + [engine._head_index + (1 if adv else 0)]
+                arr = (ctypes.c_int32 * len(recs))(*recs)
+                st = ctypes.c_void_p()
+                _lib.check(lib.nms_step_create(engine._plan, arr, len(recs), ctypes.byref(st)), "nms_step_create")
+                steps[adv] = st
             nreduce, dim = len(engine.cut_points), engine.config.dim
             nbytes = lib.nms_tp_area_bytes(nreduce, w, dim)
             own = ctypes.c_void_p()
@@ -193,17 +198,19 @@ class TensorParallel:
                 self._peer_areas.append(p)
                 areas.append(p.value)
             cfg = _lib.NmsTpConfig()
-            cfg.world, cfg.rank, cfg.dim = w, r, dim
+            cfg.world, cfg.rank, cfg.dim, cfg.vocab_offset = w, r, dim, self.info.vocab_offset
             for k, a in enumerate(areas):
                 cfg.area[k] = a
             stages = [c - 1 for c in engine.cut_points]
             sarr = (ctypes.c_int32 * len(stages))(*stages)
-            _lib.check(lib.nms_step_set_tp(step, sarr, len(stages), ctypes.byref(cfg)), "nms_step_set_tp")
+            for st in steps.values():
+                _lib.check(lib.nms_step_set_tp(st, sarr, len(stages), ctypes.byref(cfg)), "nms_step_set_tp")
         except Exception:
-            lib.nms_step_destroy(step)
+            for st in steps.values():
+                lib.nms_step_destroy(st)
             self.close()
             raise
-        engine._steps["tp"] = step
+        engine._steps.update(steps)
         engine.mode = "persistent_tp"
 
     def close(self) -> None:
