@@ -223,7 +223,7 @@ struct StepGemv {
   GemvParams g;
   int32_t lanes;    // L: lanes per row (32, 16, 8 or 4), w_pad % (16 L) == 0
   int32_t tp_send;  // tensor parallel: exchange point this stage's partial rows go to (-1: none)
-  int32_t tp_recv;  // exchange point whose summed partials replace this stage's residual addend (-1: none)
+  int32_t tp_recv;  // exchange point whose reduced vector is this stage's residual addend (-1: none)
   int32_t pad_;
 };
 
@@ -468,21 +468,13 @@ __device__ __forceinline__ void gemv_stage(const StepParams& sp, const StepGemv&
   const __half* xsrc = input_row(p);
   const bool resid = (p.prologue == kProResidNorm);
   const bool add = resid && (p.x2 != nullptr);
-  const int tpj = sg.tp_recv;  // >= 0: the addend is the sum of the ranks' partials
-  const uint32_t rtag = tpj >= 0 ? tp_tag(sp, epoch, tpj) : 0u;
   float ss = 0.f;
   if ((p.K & 7) == 0 && (reinterpret_cast<uintptr_t>(xsrc) & 15u) == 0 &&
       (!add || (reinterpret_cast<uintptr_t>(p.x2) & 15u) == 0)) {
     for (int i8 = tid; i8 < p.K / 8; i8 += NT) {
       const uint4 a = *reinterpret_cast<const uint4*>(xsrc + (size_t)i8 * 8);
       uint4 b = make_uint4(0u, 0u, 0u, 0u);
-      if (add && tpj >= 0) {
-        __half* bw = reinterpret_cast<__half*>(&b);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) bw[e] = f2h(tp_sum(sp, tpj, i8 * 8 + e, rtag));
-      } else if (add) {
-        b = *reinterpret_cast<const uint4*>(p.x2 + (size_t)i8 * 8);
-      }
+      if (add) b = *reinterpret_cast<const uint4*>(p.x2 + (size_t)i8 * 8);
       const __half* ah = reinterpret_cast<const __half*>(&a);
       const __half* bh = reinterpret_cast<const __half*>(&b);
       uint4 o;
@@ -498,7 +490,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams& sp, const StepGemv&
   } else {
     for (int i = tid; i < p.K; i += NT) {
       float v = h2f(xsrc[i]);
-      if (add) v = h2f(f2h(v + h2f(tpj >= 0 ? f2h(tp_sum(sp, tpj, i, rtag)) : p.x2[i])));
+      if (add) v = h2f(f2h(v + h2f(p.x2[i])));
       s.xs[i] = f2h(v);
       ss = fmaf(v, v, ss);
     }
@@ -957,20 +949,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     if (tr != nullptr && tid == 0) tr[cta] = global_timer_ns();
     if (tp_j >= 0) {
       // Tensor-parallel exchange point: the partial rows went out in the
-      // epilogue and carry their own arrival tags, so no barrier here: the
-      // next stage's prologue waits for exactly the words it adds.  This GPU's
-      // grid arrival s is still counted, keeping later barrier targets.
-      if (s + 1 < sp.nstages) {
-        grid_arrive(sp.bar_count);
-        if (s_kind[s + 1] == kStageGemv) gemv_pre_smem(s_g[gn & 1], ncta, act, &s_pre_bar, pre_uses);
-      } else if (tp_out != nullptr) {
-        // Last stage: the reduced vector is the step's output (read by the
-        // next launch), each CTA writing a slice.
+      // epilogue carrying their arrival tags.  Each CTA sums its slice of the
+      // vector over the ranks (rank order) into the stage's own output, then
+      // the usual grid barrier: the next stage reads the reduced vector as
+      // its residual addend, like the single-GPU step.
+      {
         const uint32_t tag = tp_tag(sp, epoch, tp_j);
         const int i0 = (int)(((int64_t)cta * sp.tp_dim) / ncta), i1 = (int)(((int64_t)(cta + 1) * sp.tp_dim) / ncta);
         for (int i = i0 + tid; i < i1; i += kStepThreads) tp_out[i] = f2h(tp_sum(sp, tp_j, i, tag));
       }
-      __syncthreads();
+      if (s + 1 < sp.nstages) {
+        grid_arrive(sp.bar_count);
+        if (s_kind[s + 1] == kStageGemv) gemv_pre_smem(s_g[gn & 1], ncta, act, &s_pre_bar, pre_uses);
+        if (!grid_wait(sp.bar_count, ncta, (unsigned)s)) {
+          asm volatile("cp.async.wait_all;" ::: "memory");
+          if (tid == 0 && pre_uses > 0u) mbar_wait_bounded(&s_pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);
+          __syncthreads();
+          return;
+        }
+      }
       if (tr != nullptr && cta == 0 && tid == 0) tr[ncta] = global_timer_ns();
     } else if (s + 1 < sp.nstages) {
       grid_arrive(sp.bar_count);  // includes __syncthreads: the stored parameters are visible
