@@ -220,11 +220,30 @@ def run_reference_arm(args, world: int, rank: int) -> None:
                          "sample": r["sample"]},
         "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    """The one JSON line on the process's original stdout."""
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
 
 
 def main():
+    global _JSON_FD
     args = parse_args()
+    # Libraries (NCCL's version banner, warnings) may write to file
+    # descriptor 1: send it to stderr so stdout carries only the JSON line.
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -244,8 +263,6 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
-            os.environ["NCCL_DEBUG"] = "WARN"  # no version banner: stdout carries the one JSON line
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     nm = None if args.nm == "dense" else tuple(int(v) for v in args.nm.split(":"))
     cfg = model_config(args)
@@ -436,7 +453,7 @@ def main():
             "build_s": round(build_s, 1),
             "device_error": dev_err,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         tp.close()
