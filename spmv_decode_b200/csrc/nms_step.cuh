@@ -783,39 +783,70 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, 
   }
   __syncthreads();
   if (!S.last) return;
-  // Last split of this head: combine every split's state (read through L2,
-  // all loads of a thread independent so they overlap).
+  // Last split of this head: combine every split's state, read through L2.
+  // The partial outputs a thread weights are loaded together with the
+  // (m, l) pairs (one round trip), and the split weights of a query head are
+  // computed by one lane per split with shuffles.
   const float* hp = part + (size_t)kvh * p.splits * GM * STRIDE;
-  float* fw = &S.so[0][0];                 // reuse: per (split, head) weight exp(m_r - M) / L
-  float* mlr = &S.sq[0][0];                // reuse: per (split, head) (m, l)
-  for (int i = tid; i < p.splits * G; i += NT) {
-    const int r = i / G, g = i - r * G;
-    mlr[2 * (r * GM + g)] = __ldcg(hp + ((size_t)r * GM + g) * STRIDE);
-    mlr[2 * (r * GM + g) + 1] = __ldcg(hp + ((size_t)r * GM + g) * STRIDE + 1);
-  }
-  __syncthreads();
-  if (tid < G) {
-    const int g = tid;
-    float M = -INFINITY;
-    for (int r = 0; r < p.splits; ++r) M = fmaxf(M, mlr[2 * (r * GM + g)]);
-    float Lsum = 0.f;
-    for (int r = 0; r < p.splits; ++r) {
-      const float mr = mlr[2 * (r * GM + g)];
-      const float f = (mr == -INFINITY) ? 0.f : expf(mr - M);
-      fw[r * GM + g] = f;
-      Lsum = fmaf(mlr[2 * (r * GM + g) + 1], f, Lsum);
-    }
-    const float inv = 1.0f / Lsum;
-    for (int r = 0; r < p.splits; ++r) fw[r * GM + g] *= inv;
-  }
-  __syncthreads();
-  for (int i = tid; i < G * D; i += NT) {
+  float* fw = &S.so[0][0];   // per (split, head) weight exp(m_r - M) / L
+  constexpr int IPT = (kAttnMaxGroup * D + NT - 1) / NT;  // output items per thread
+  float ov[IPT][kMaxSplits];
+#pragma unroll
+  for (int k = 0; k < IPT; ++k) {
+    const int i = tid + k * NT;
     const int g = i / D, d = i - g * D;
-    float O = 0.f;
 #pragma unroll
     for (int r = 0; r < kMaxSplits; ++r)
-      if (r < p.splits) O = fmaf(__ldcg(hp + ((size_t)r * GM + g) * STRIDE + 2 + d), fw[r * GM + g], O);
-    p.y[(size_t)(kvh * G + g) * D + d] = f2h(O);
+      ov[k][r] = (i < G * D && r < p.splits) ? __ldcg(hp + ((size_t)r * GM + g) * STRIDE + 2 + d) : 0.f;
+  }
+  const bool fast = (p.splits & (p.splits - 1)) == 0 && p.splits <= kWarp && G * p.splits <= NT;
+  if (fast) {
+    // Lane group of `splits` lanes per query head: i = g * splits + r.
+    const int i = tid, g = i / p.splits, r = i - g * p.splits;
+    const bool on = i < G * p.splits;
+    const float mr = on ? __ldcg(hp + ((size_t)r * GM + g) * STRIDE) : -INFINITY;
+    const float lr = on ? __ldcg(hp + ((size_t)r * GM + g) * STRIDE + 1) : 0.f;
+    float M = mr;
+    for (int o = p.splits >> 1; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float f = (mr == -INFINITY) ? 0.f : expf(mr - M);
+    float Ls = lr * f;
+    for (int o = p.splits >> 1; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
+    if (on) fw[r * GM + g] = f / Ls;
+  } else {
+    float* mlr = &S.sq[0][0];  // per (split, head) (m, l)
+    for (int i = tid; i < p.splits * G; i += NT) {
+      const int r = i / G, g = i - r * G;
+      mlr[2 * (r * GM + g)] = __ldcg(hp + ((size_t)r * GM + g) * STRIDE);
+      mlr[2 * (r * GM + g) + 1] = __ldcg(hp + ((size_t)r * GM + g) * STRIDE + 1);
+    }
+    __syncthreads();
+    if (tid < G) {
+      const int g = tid;
+      float M = -INFINITY;
+      for (int r = 0; r < p.splits; ++r) M = fmaxf(M, mlr[2 * (r * GM + g)]);
+      float Lsum = 0.f;
+      for (int r = 0; r < p.splits; ++r) {
+        const float mr = mlr[2 * (r * GM + g)];
+        const float f = (mr == -INFINITY) ? 0.f : expf(mr - M);
+        fw[r * GM + g] = f;
+        Lsum = fmaf(mlr[2 * (r * GM + g) + 1], f, Lsum);
+      }
+      const float inv = 1.0f / Lsum;
+      for (int r = 0; r < p.splits; ++r) fw[r * GM + g] *= inv;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < IPT; ++k) {
+    const int i = tid + k * NT;
+    if (i < G * D) {
+      const int g = i / D, d = i - g * D;
+      float O = 0.f;
+#pragma unroll
+      for (int r = 0; r < kMaxSplits; ++r)
+        if (r < p.splits) O = fmaf(ov[k][r], fw[r * GM + g], O);
+      p.y[(size_t)(kvh * G + g) * D + d] = f2h(O);
+    }
   }
 }
 
