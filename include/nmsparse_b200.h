@@ -253,7 +253,7 @@ int nms_plan_launch(const nms_plan* plan, int32_t begin, int32_t end, void* stre
 /* ---------------------------------------------------------------------------
  * Persistent decode step: the GEMV and attention records listed in
  * `records` (plan indices, in execution order) run as stages of ONE
- * cooperative kernel (one 512-thread CTA per SM) separated by in-kernel grid
+ * cooperative kernel (one 640-thread CTA per SM) separated by in-kernel grid
  * barriers; every warp streams its weights through a shared-memory ring whose
  * copies run ahead across stage boundaries.  Replaces the per-kernel decode
  * step of the plan (and, like it, the reference's compiled + graph-captured
