@@ -51,7 +51,8 @@ int nms_num_sms(int* out);
  * hanging (1 = bulk-copy wait timed out, 2 = attention position outside the
  * KV cache, 3 = persistent-step grid barrier timed out, 4 = persistent-step
  * weight-ring slot never refilled, 5 = persistent-step weight-ring chunk does
- * not fit its stage; the kernel skipped its work).  Synchronizes the current
+ * not fit its stage, 6 = prefill GEMM copy or tensor-core wait timed out; the
+ * kernel skipped its work).  Synchronizes the current
  * device.  With clear != 0 the word is reset to 0. */
 int nms_device_error(int* code_out, int clear);
 
@@ -93,6 +94,29 @@ int nms_unpack_f16(const void* packed, void* mat_data, int64_t w, int64_t h, int
 int nms_gemv_packed_f16(const void* vec, const void* packed, const void* mat_index, void* out, int64_t K,
                         int64_t w, int64_t w_pad, int64_t h, int32_t block_width, int32_t vec_width,
                         void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Batch > 1 (prefill) sparse GEMM on the packed layout.  The reference sends
+ * every multi-token input to a dense F.linear with the unpruned weight
+ * (src/spmv/nmsparse_linear.py:55-68) and its op refuses rows != 1
+ * (src/spmv/nmsparse_op.py:84-87); this computes the sparse layer itself:
+ *   out[t, r] = sum_j packed[r, j] * x[t, (j/N)*M + mat_index[j/N, j%N]]
+ * for T tokens: x [T, K] (x_dtype: fp16, bf16 or fp32, converted to fp16 as
+ * the reference op converts its input), packed [h, w_pad] fp16 (16-byte
+ * aligned), out [T, h] fp16, fp32 accumulation on the tensor cores.
+ * workspace: caller-owned device memory of nms_gemm_workspace_bytes(T, w_pad,
+ * h) bytes (256-byte aligned; no initial contents needed).  Launches two
+ * kernels on `stream` (gather + GEMM) and is CUDA-graph capturable; launches
+ * that share a workspace must be ordered on one stream.  The result does not
+ * depend on launch timing (split-K partials are summed in a fixed order).
+ * ------------------------------------------------------------------------- */
+#define NMS_DTYPE_F16 0
+#define NMS_DTYPE_BF16 1
+#define NMS_DTYPE_F32 2
+int nms_gemm_workspace_bytes(int64_t T, int64_t w_pad, int64_t h, int64_t* bytes_out);
+int nms_gemm_packed_f16(const void* x, int32_t x_dtype, const void* packed, const void* mat_index, void* out,
+                        int64_t T, int64_t K, int64_t w, int64_t w_pad, int64_t h, int32_t block_width,
+                        int32_t vec_width, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Fused decode launches (packed layout).  One launch covers several linears

@@ -6,6 +6,8 @@ numpy restatement of the reference's shared-mask N:M sparse GEMV:
   matrix with mat_data scattered to columns g*M + mat_index[g, i].
 * gemv_fp32     -- microbench_triton_torchmv.py:383-386: torch.mv of that
   matrix and the vector, both in fp32 (the reference's correctness oracle).
+* gemm_fp32     -- the same product for T tokens, row by row (the
+  multi-token sparse layer the reference lacks, src/spmv/nmsparse_linear.py:55-68).
 * gemv_kernel_order -- triton_spmv.py:81-108 loop order for one program
   (group by group, kept slot by kept slot, fp32 fused multiply-add); small
   cases only.
@@ -54,6 +56,17 @@ def gemv_fp32(x: np.ndarray, mat_data: np.ndarray, mat_index: np.ndarray, K: int
     cols = gather_columns(mat_index, m)
     xc = x[cols]  # identical to the dense product: zero columns contribute nothing
     return as_f16(mat_data).astype(np.float32).T @ xc
+
+
+def gemm_fp32(X: np.ndarray, mat_data: np.ndarray, mat_index: np.ndarray, K: int, m: int) -> np.ndarray:
+    """fp32 reference output [T, h] for T tokens: gemv_fp32 of every row of X.
+
+    The reference has no multi-token sparse product (its linear sends T > 1
+    to a dense F.linear, src/spmv/nmsparse_linear.py:55-68), so each token's
+    row is defined as its single-token product (microbench_triton_torchmv.py:383-386)."""
+    X = as_f16(X).reshape(-1, K).astype(np.float32)
+    cols = gather_columns(mat_index, m)
+    return X[:, cols] @ as_f16(mat_data).astype(np.float32)
 
 
 def gemv_kernel_order(x: np.ndarray, mat_data: np.ndarray, mat_index: np.ndarray, m: int) -> np.ndarray:

@@ -32,6 +32,9 @@ NMS_FLAG_PDL = 1
 NMS_FLAG_DENSE = 2
 NMS_ROPE_INTERLEAVED = 0
 NMS_ROPE_HALF = 1
+NMS_DTYPE_F16 = 0
+NMS_DTYPE_BF16 = 1
+NMS_DTYPE_F32 = 2
 
 # Every exported symbol of include/nmsparse_b200.h (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
@@ -42,6 +45,8 @@ EXPORTED_SYMBOLS = (
     "nms_device_error",
     "nms_gemv_f16",
     "nms_gemv_rowwise_f16",
+    "nms_gemm_workspace_bytes",
+    "nms_gemm_packed_f16",
     "nms_packed_row_stride",
     "nms_pack_f16",
     "nms_unpack_f16",
@@ -164,6 +169,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "nms_device_error": (I32, [ctypes.POINTER(I32), I32]),
         "nms_gemv_f16": (I32, [P, P, P, P, I64, I64, I64, I32, I32, P]),
         "nms_gemv_rowwise_f16": (I32, [P, P, P, P, I64, I64, I64, I32, I32, P]),
+        "nms_gemm_workspace_bytes": (I32, [I64, I64, I64, ctypes.POINTER(c_i64)]),
+        "nms_gemm_packed_f16": (I32, [P, I32, P, P, P, I64, I64, I64, I64, I64, I32, I32, P, I64, P]),
         "nms_packed_row_stride": (I64, [I64]),
         "nms_pack_f16": (I32, [P, P, I64, I64, I64, P]),
         "nms_unpack_f16": (I32, [P, P, I64, I64, I64, P]),

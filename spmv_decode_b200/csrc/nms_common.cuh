@@ -25,6 +25,7 @@ enum DeviceError : int {
   kDevBarrierTimeout = 3,    // persistent step: a grid barrier wait ran past its limit
   kDevRingTimeout = 4,       // persistent step: a weight-ring slot was never refilled
   kDevRingMismatch = 5,      // persistent step: a weight-ring chunk does not fit its stage
+  kDevMmaTimeout = 6,        // prefill GEMM: a copy or tensor-core wait ran past its limit
 };
 __device__ int g_device_error;
 

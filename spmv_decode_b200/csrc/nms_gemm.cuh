@@ -1,0 +1,341 @@
+// Batch > 1 (prefill) shared-mask N:M sparse GEMM on the packed layout.
+//
+// The reference runs every multi-token input through a dense F.linear
+// (src/spmv/nmsparse_linear.py:55-68); its op refuses rows != 1
+// (src/spmv/nmsparse_op.py:84-87).  With one mask shared by all output rows
+// the sparse product is a dense GEMM over the compressed width w = K*N/M:
+//   out[t, r] = sum_j packed[r, j] * xc[t, j],
+//   xc[t, j]  = x[t, (j / N) * M + mat_index[j / N, j % N]]
+// (the same sum as the GEMV, src/spmv/triton_spmv.py:81-108, for every t).
+//
+// Two kernels:
+//   gather_xc_kernel  builds xc [T, w_pad] fp16 (zeros past w), casting x
+//                     (fp16, bf16 or fp32) to fp16 the way the reference op
+//                     casts its input.
+//   gemm_nm_kernel    one CTA per (128 rows of h, BN tokens, k-split) tile on
+//                     the 5th-generation tensor cores: TMA (128-byte swizzle)
+//                     streams packed rows and xc rows into a ring of shared
+//                     memory stages, one thread issues tcgen05.mma (M=128,
+//                     N=BN, K=16, fp16 x fp16 -> fp32) into a TMEM
+//                     accumulator, and all four warps read it back with
+//                     tcgen05.ld.  Both operands are K-major: row r of the
+//                     packed matrix is A's row, token t of xc is B's row.
+//
+// Split-K (only when even 32-token tiles leave SMs idle): the S k-splits of
+// one tile run as one thread-block cluster.  Each CTA stages its fp32
+// partial tile in its own shared memory; after a cluster barrier, CTA r sums
+// columns [r*BN/S, (r+1)*BN/S) of all S partials over distributed shared
+// memory in split order (so the result does not depend on timing) and writes
+// them; a second cluster barrier keeps every partial alive until all reads
+// are done.
+//
+// Every mbarrier wait is bounded (kGemmWaitNs); a wait that runs out records
+// kDevMmaTimeout in the device error word and the CTA finishes without
+// issuing further copies or MMAs.
+#pragma once
+
+#include <cuda.h>  // CUtensorMap (type only; the encoder is fetched at run time)
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "nms_common.cuh"
+
+namespace nms {
+
+constexpr int kGemmBM = 128;          // rows of h per tile (UMMA M)
+constexpr int kGemmBK = 64;           // compressed columns per stage: one 128-byte swizzle row
+constexpr int kGemmThreads = 128;     // 4 warps: TMA producer, MMA issuer, TMEM owner, all epilogue
+constexpr int kGemmMaxStages = 8;
+constexpr int kGemmMaxBN = 256;       // UMMA N limit and TMA box limit
+constexpr int kGemmOutPitch = kGemmBM + 8;  // halves per staged output row (272 B, 16-B aligned)
+constexpr uint64_t kGemmWaitNs = 200ull * 1000 * 1000;
+
+struct GemmParams {
+  __half* out;           // [T, h] fp16
+  int32_t T, h;
+  int32_t bn;            // tokens per tile (multiple of 16, <= 256)
+  int32_t kblocks;       // w_pad / 64
+  int32_t splits;        // k-splits per tile (<= kblocks, <= 8): the cluster size along z
+  int32_t stages;        // shared-memory ring depth
+  uint32_t idesc;        // tcgen05 instruction descriptor
+  uint32_t tmem_cols;    // TMEM columns allocated (power of 2, >= 32, >= bn)
+  int32_t vec_out;       // 16-byte output stores allowed (h % 8 == 0, out aligned)
+};
+
+// ---------------------------------------------------------------------------
+// Gather: one thread per 8 consecutive compressed columns of one token.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(float v) { return v; }
+
+template <typename TX>
+__global__ void __launch_bounds__(256) gather_xc_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ idx,
+                                                        __half* __restrict__ xc, int32_t T, int32_t K, int32_t w,
+                                                        int32_t w_pad, int32_t n, int32_t m) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int32_t chunks = w_pad >> 3;
+  if (gid >= (int64_t)T * chunks) return;
+  const int32_t t = (int32_t)(gid / chunks);
+  const int32_t j0 = (int32_t)(gid - (int64_t)t * chunks) * 8;
+  const TX* xr = x + (int64_t)t * K;
+  __align__(16) __half v[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int32_t j = j0 + q;
+    float f = 0.f;
+    if (j < w) f = to_f32(xr[(j / n) * m + idx[j]]);
+    v[q] = __float2half_rn(f);
+  }
+  *reinterpret_cast<uint4*>(xc + (int64_t)t * w_pad + j0) = *reinterpret_cast<const uint4*>(v);
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMA primitives (cta_group::1, this CTA only).
+// ---------------------------------------------------------------------------
+
+// Shared-memory matrix descriptor: K-major operand tile whose rows are 128
+// bytes (64 fp16) with the 128-byte swizzle TMA writes; groups of 8 rows are
+// 1024 bytes apart (stride byte offset), the leading byte offset is unused
+// for swizzled K-major layouts (1), descriptor version 1, swizzle mode 2.
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, fp16 A and B, both
+// K-major, N = bn, M = 128.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int m, int bn) {
+  return (1u << 4) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma this thread issued before it has
+// completed (and so has finished reading its shared-memory operands).
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// 16 consecutive fp32 accumulator columns of this thread's TMEM lane; the
+// wait is in the same asm block so no use of the registers can be scheduled
+// before the load has landed.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if (global_timer_ns() - t0 > kGemmWaitNs) {
+      set_device_error(kDevMmaTimeout);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The GEMM.  grid = (m tiles, n tiles, splits), 128 threads, dynamic shared
+// memory = 1 KB alignment slack + stages x (16 KB A + bn x 128 B B).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_nm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const GemmParams p) {
+  extern __shared__ uint8_t gemm_smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kGemmMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kGemmMaxStages];
+  __shared__ __align__(8) uint64_t accum_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int32_t s_abort, s_issued, s_consumed;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * p.bn, split = blockIdx.z;
+  const int kb0 = (int)((int64_t)p.kblocks * split / p.splits);
+  const int kb1 = (int)((int64_t)p.kblocks * (split + 1) / p.splits);
+  const int nk = kb1 - kb0;
+
+  const uint32_t raw = smem_u32(gemm_smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t a_bytes = kGemmBM * 128u, b_bytes = (uint32_t)p.bn * 128u;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&accum_bar, 1);
+    s_abort = 0;
+    s_issued = 0;
+    s_consumed = 0;
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 2) tmem_alloc(&tmem_slot, p.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer.
+    int i = 0;
+    for (; i < nk; ++i) {
+      const int s = i % p.stages;
+      const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
+      if (!gemm_wait(&empty_bar[s], ph ^ 1u)) {
+        atomicExch(&s_abort, 1);
+        break;
+      }
+      if (*(volatile int32_t*)&s_abort) break;
+      const uint32_t sa = base + (uint32_t)s * stage_bytes;
+      const int32_t kx = (kb0 + i) * kGemmBK;
+      mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
+      tma_load_2d(sa, &tm_a, kx, m0, smem_u32(&full_bar[s]));
+      tma_load_2d(sa + a_bytes, &tm_b, kx, n0, smem_u32(&full_bar[s]));
+    }
+    s_issued = i;
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: 4 MMAs (K = 16 each) per 64-column stage; advancing K by 16
+    // fp16 inside the 128-byte swizzle row is +32 bytes on the start address.
+    int i = 0;
+    for (; i < nk; ++i) {
+      const int s = i % p.stages;
+      const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
+      if (!gemm_wait(&full_bar[s], ph)) {
+        atomicExch(&s_abort, 1);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = base + (uint32_t)s * stage_bytes;
+      const uint64_t da = umma_desc_k_sw128(sa), db = umma_desc_k_sw128(sa + a_bytes);
+#pragma unroll
+      for (int kk = 0; kk < kGemmBK / 16; ++kk)
+        umma_f16(tmem, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), p.idesc, (i | kk) != 0 ? 1u : 0u);
+      umma_commit(smem_u32(&empty_bar[s]));
+    }
+    s_consumed = i;
+    umma_commit(smem_u32(&accum_bar));
+  }
+  __syncwarp();
+
+  // ---- epilogue: TMEM lane (32 * warp + lane) holds tile row m0 + that ----
+  const bool acc_ok = gemm_wait(&accum_bar, 0);
+  tc_fence_after();
+  const int row = warp * 32 + lane;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  __half* out_s = reinterpret_cast<__half*>(gemm_smem_raw + (base - raw));
+  const int nchunks = p.bn >> 4;
+  if (p.splits > 1) {
+    // Partial tile -> own shared memory, column-major [bn][128] fp32.
+    float* part_s = reinterpret_cast<float*>(gemm_smem_raw + (base - raw));
+    for (int c = 0; c < nchunks; ++c) {
+      float v[16];
+      tmem_ld16(trow + (uint32_t)(c * 16), v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) part_s[(c * 16 + j) * kGemmBM + row] = v[j];
+    }
+    cluster_sync_all();
+    const int r = (int)cluster_ctarank();
+    const int c0 = p.bn * r / p.splits, c1 = p.bn * (r + 1) / p.splits;
+    const bool row_ok = acc_ok && m0 + row < p.h;
+    for (int col = c0; col < c1; ++col) {
+      float acc = 0.f;
+      for (int s = 0; s < p.splits; ++s) acc += ld_dsmem_f32(part_s + col * kGemmBM + row, (uint32_t)s);
+      if (row_ok && n0 + col < p.T) p.out[(int64_t)(n0 + col) * p.h + m0 + row] = __float2half_rn(acc);
+    }
+    cluster_sync_all();
+  } else {
+    for (int c = 0; c < nchunks; ++c) {
+      float v[16];
+      tmem_ld16(trow + (uint32_t)(c * 16), v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out_s[(c * 16 + j) * kGemmOutPitch + row] = __float2half_rn(v[j]);
+    }
+  }
+  __syncthreads();
+  if (p.splits == 1 && acc_ok) {
+    const int rows_valid = min(p.bn, p.T - n0);
+    const int cols_valid = min(kGemmBM, p.h - m0);
+    for (int q = threadIdx.x; q < p.bn * (kGemmBM / 8); q += kGemmThreads) {
+      const int t = q >> 4, c8 = (q & 15) * 8;
+      if (t >= rows_valid || c8 >= cols_valid) continue;
+      __half* dst = p.out + (int64_t)(n0 + t) * p.h + m0 + c8;
+      const __half* src = out_s + t * kGemmOutPitch + c8;
+      if (p.vec_out && c8 + 8 <= cols_valid) {
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      } else {
+        const int e_end = min(8, cols_valid - c8);
+        for (int e = 0; e < e_end; ++e) dst[e] = src[e];
+      }
+    }
+  }
+
+  // ---- teardown ----
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && s_abort) {
+    // Let copies still in flight land before the CTA's shared memory is
+    // released (each wait is bounded).
+    for (int i = s_consumed; i < s_issued; ++i) {
+      if (!gemm_wait(&full_bar[i % p.stages], (uint32_t)(i / p.stages) & 1u)) break;
+    }
+  }
+  if (warp == 2) tmem_dealloc(tmem, p.tmem_cols);
+}
+
+}  // namespace nms

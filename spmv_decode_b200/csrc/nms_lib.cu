@@ -12,6 +12,7 @@
 // parameters, grid, shared memory, launch attributes).  The direct entry
 // points launch the record immediately; the plan API stores records and
 // replays them (nms_plan_launch), which is the decode-step executor.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -27,6 +28,7 @@
 
 #include "nms_common.cuh"
 #include "nms_decode.cuh"
+#include "nms_gemm.cuh"
 #include "nms_gemv.cuh"
 #include "nms_step.cuh"
 
@@ -58,6 +60,7 @@ struct DeviceInfo {
   int num_sms = 0;
   size_t max_smem_optin = 0;
   size_t step_smem_max = 0;
+  size_t gemm_smem_max = 0;  // dynamic shared memory gemm_nm_kernel may use
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -107,6 +110,15 @@ int device_info(const DeviceInfo** out) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem - (int)fa.sharedSizeBytes);
       if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(decode_step_kernel)");
       d.step_smem_max = std::min(d.step_smem_max, (size_t)smem - fa.sharedSizeBytes);
+    }
+    {
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, (const void*)nms::gemm_nm_kernel);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncGetAttributes(gemm_nm_kernel)");
+      d.gemm_smem_max = (size_t)smem - fa.sharedSizeBytes;
+      e = cudaFuncSetAttribute((const void*)nms::gemm_nm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)d.gemm_smem_max);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(gemm_nm_kernel)");
     }
     e = cudaFuncSetAttribute((const void*)nms::attention_decode_kernel,
                              cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -477,6 +489,106 @@ int noalloc_scratch(unsigned char** out) {
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Prefill GEMM (nms_gemm.cuh): tile plan, workspace layout, tensor maps.
+// ---------------------------------------------------------------------------
+struct GemmPlan {
+  int32_t m_tiles = 0, n_tiles = 0, bn = 0, splits = 1, stages = 0, kblocks = 0;
+  size_t smem = 0;
+  int64_t total = 0;  // workspace bytes: xc [T, w_pad] fp16
+};
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Tokens are split into ceil(T / 256) equal tiles (UMMA N <= 256, a multiple
+// of 16); rows of h into 128-row tiles.  While the tiles fill less than half
+// the SMs, the token tiles are halved (down to 32 tokens: the weight tile is
+// then re-read by the CTAs of one row block, mostly from L2).  If the tiles
+// still leave SMs idle, the compressed width is split too: at most 8 ways (the
+// portable cluster size), at least one 64-column stage per split.  The ring
+// takes as many stages (<= 8) as shared memory holds.
+int gemm_plan(int64_t T, int64_t w_pad, int64_t h, int num_sms, size_t smem_max, GemmPlan* g) {
+  g->n_tiles = (int32_t)((T + nms::kGemmMaxBN - 1) / nms::kGemmMaxBN);
+  g->bn = (int32_t)std::max<int64_t>(16, round_up((T + g->n_tiles - 1) / g->n_tiles, 16));
+  g->m_tiles = (int32_t)((h + nms::kGemmBM - 1) / nms::kGemmBM);
+  g->kblocks = (int32_t)(w_pad / nms::kGemmBK);
+  while (g->bn >= 64 && (int64_t)g->m_tiles * g->n_tiles * 2 <= num_sms) {
+    g->bn = (int32_t)round_up(g->bn / 2, 16);
+    g->n_tiles = (int32_t)((T + g->bn - 1) / g->bn);
+  }
+  const int64_t tiles = (int64_t)g->m_tiles * g->n_tiles;
+  g->splits = 1;
+  if (tiles < num_sms) {
+    g->splits = (int32_t)std::min<int64_t>({(int64_t)num_sms / tiles, (int64_t)g->kblocks, 8});
+    if (g->splits < 1) g->splits = 1;
+  }
+  const size_t stage = (size_t)nms::kGemmBM * 128 + (size_t)g->bn * 128;
+  const size_t avail = smem_max > 1024 ? smem_max - 1024 : 0;
+  g->stages = (int32_t)std::min<size_t>(nms::kGemmMaxStages, avail / stage);
+  if (g->stages < 2) return fail(NMS_ERR_NOT_IMPLEMENTED, "gemm: %zu B of shared memory holds fewer than 2 stages", smem_max);
+  g->smem = 1024 + (size_t)g->stages * stage;
+  // Epilogue staging reuses the ring: fp16 output rows, or the fp32 partial.
+  const size_t staging = g->splits > 1 ? (size_t)g->bn * nms::kGemmBM * 4 : (size_t)g->bn * nms::kGemmOutPitch * 2;
+  if (staging > (size_t)g->stages * stage)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "gemm: epilogue staging of %zu B exceeds the ring", staging);
+  g->total = round_up(T * w_pad * 2, 256);
+  return NMS_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_tiled_fn(EncodeTiledFn* out) {
+  static std::mutex mu;
+  static EncodeTiledFn fn = nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+    if (q != cudaDriverEntryPointSuccess || p == nullptr)
+      return fail(NMS_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  *out = fn;
+  return NMS_OK;
+}
+
+// 2-D fp16 tensor map over a row-major [rows, cols] matrix: boxes of
+// 64 columns (128 bytes) x box_rows rows, 128-byte swizzle, zero fill outside.
+int encode_k_major(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int32_t box_rows) {
+  EncodeTiledFn fn = nullptr;
+  int rc = encode_tiled_fn(&fn);
+  if (rc) return rc;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)nms::kGemmBK, (cuuint32_t)box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NMS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return NMS_OK;
+}
+
+int gemm_check_shape(int64_t T, int64_t K, int64_t w, int64_t w_pad, int64_t h, int32_t block_width,
+                     int32_t vec_width) {
+  if (T <= 0 || T > (1 << 24)) return fail(NMS_ERR_VALUE, "T=%lld must be in [1, 2^24]", (long long)T);
+  if (h <= 0 || h > (1ll << 30)) return fail(NMS_ERR_VALUE, "h=%lld out of range", (long long)h);
+  if (block_width <= 0 || vec_width <= 0) return fail(NMS_ERR_VALUE, "N and M must be positive");
+  if (block_width > vec_width || vec_width > 256)
+    return fail(NMS_ERR_VALUE, "N=%d, M=%d: need N <= M <= 256", block_width, vec_width);
+  if (w <= 0 || w % block_width != 0) return fail(NMS_ERR_VALUE, "w=%lld must be divisible by N=%d", (long long)w, block_width);
+  if (K != (w / block_width) * vec_width)
+    return fail(NMS_ERR_VALUE, "K=%lld must equal (w/N)*M=%lld", (long long)K, (long long)((w / block_width) * vec_width));
+  if (K > (1ll << 30)) return fail(NMS_ERR_VALUE, "K=%lld out of range", (long long)K);
+  if (w_pad != nms_packed_row_stride(w))
+    return fail(NMS_ERR_VALUE, "w_pad=%lld must be %lld", (long long)w_pad, (long long)nms_packed_row_stride(w));
+  return NMS_OK;
+}
 
 struct nms_plan {
   std::vector<LaunchRec> recs;
@@ -1056,6 +1168,98 @@ int nms_step_destroy(nms_step* step) {
   if (step->dev_mem) cudaFree(step->dev_mem);
   cudaSetDevice(cur);
   delete step;
+  return NMS_OK;
+}
+
+int nms_gemm_workspace_bytes(int64_t T, int64_t w_pad, int64_t h, int64_t* bytes_out) {
+  if (bytes_out == nullptr) return fail(NMS_ERR_VALUE, "null pointer argument");
+  if (T <= 0 || h <= 0 || w_pad <= 0 || w_pad % 64 != 0)
+    return fail(NMS_ERR_VALUE, "T, h must be positive and w_pad a positive multiple of 64");
+  const DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  GemmPlan g;
+  rc = gemm_plan(T, w_pad, h, dev->num_sms, dev->gemm_smem_max, &g);
+  if (rc) return rc;
+  *bytes_out = g.total;
+  return NMS_OK;
+}
+
+int nms_gemm_packed_f16(const void* x, int32_t x_dtype, const void* packed, const void* mat_index, void* out,
+                        int64_t T, int64_t K, int64_t w, int64_t w_pad, int64_t h, int32_t block_width,
+                        int32_t vec_width, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!x || !packed || !mat_index || !out || !workspace) return fail(NMS_ERR_VALUE, "null pointer argument");
+  if (x_dtype != NMS_DTYPE_F16 && x_dtype != NMS_DTYPE_BF16 && x_dtype != NMS_DTYPE_F32)
+    return fail(NMS_ERR_TYPE, "x_dtype=%d is not NMS_DTYPE_F16/BF16/F32", x_dtype);
+  int rc = gemm_check_shape(T, K, w, w_pad, h, block_width, vec_width);
+  if (rc) return rc;
+  if (!aligned(packed, 16)) return fail(NMS_ERR_VALUE, "packed must be 16-byte aligned");
+  if (!aligned(workspace, 256)) return fail(NMS_ERR_VALUE, "workspace must be 256-byte aligned");
+  const int esize = x_dtype == NMS_DTYPE_F32 ? 4 : 2;
+  if (!aligned(x, esize)) return fail(NMS_ERR_VALUE, "x is not aligned to its element size");
+  if (!aligned(out, 2)) return fail(NMS_ERR_VALUE, "out must be 2-byte aligned");
+  const DeviceInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  GemmPlan g;
+  rc = gemm_plan(T, w_pad, h, dev->num_sms, dev->gemm_smem_max, &g);
+  if (rc) return rc;
+  if (workspace_bytes < g.total)
+    return fail(NMS_ERR_VALUE, "workspace of %lld bytes < %lld required (nms_gemm_workspace_bytes)",
+                (long long)workspace_bytes, (long long)g.total);
+  __half* xc = static_cast<__half*>(workspace);
+
+  CUtensorMap tm_a, tm_b;
+  rc = encode_k_major(&tm_a, packed, h, w_pad, nms::kGemmBM);
+  if (rc) return rc;
+  rc = encode_k_major(&tm_b, xc, T, w_pad, g.bn);
+  if (rc) return rc;
+
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned gblocks = (unsigned)((T * (w_pad / 8) + 255) / 256);
+  const uint8_t* idx = static_cast<const uint8_t*>(mat_index);
+  if (x_dtype == NMS_DTYPE_F16)
+    nms::gather_xc_kernel<__half><<<gblocks, 256, 0, st>>>(static_cast<const __half*>(x), idx, xc, (int32_t)T,
+                                                           (int32_t)K, (int32_t)w, (int32_t)w_pad, block_width,
+                                                           vec_width);
+  else if (x_dtype == NMS_DTYPE_BF16)
+    nms::gather_xc_kernel<__nv_bfloat16><<<gblocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), idx, xc,
+                                                                  (int32_t)T, (int32_t)K, (int32_t)w, (int32_t)w_pad,
+                                                                  block_width, vec_width);
+  else
+    nms::gather_xc_kernel<float><<<gblocks, 256, 0, st>>>(static_cast<const float*>(x), idx, xc, (int32_t)T,
+                                                          (int32_t)K, (int32_t)w, (int32_t)w_pad, block_width,
+                                                          vec_width);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "gather_xc_kernel launch");
+
+  nms::GemmParams p;
+  p.out = static_cast<__half*>(out);
+  p.T = (int32_t)T;
+  p.h = (int32_t)h;
+  p.bn = g.bn;
+  p.kblocks = g.kblocks;
+  p.splits = g.splits;
+  p.stages = g.stages;
+  p.idesc = nms::umma_idesc_f16_f32(nms::kGemmBM, g.bn);
+  p.tmem_cols = 32;
+  while ((int32_t)p.tmem_cols < g.bn) p.tmem_cols <<= 1;
+  p.vec_out = (h % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)g.m_tiles, (unsigned)g.n_tiles, (unsigned)g.splits);
+  cfg.blockDim = dim3(nms::kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = g.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)g.splits;  // the k-splits of one tile form a cluster
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, nms::gemm_nm_kernel, tm_a, tm_b, p);
+  if (e != cudaSuccess) return fail_cuda(e, "gemm_nm_kernel launch");
   return NMS_OK;
 }
 

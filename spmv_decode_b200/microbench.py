@@ -20,7 +20,12 @@ For every shape (out x in) and N:M ratio: seeded synthetic shared-mask weights
 * ``rowwise``  -- the per-row layout (top-|w| per row and
                   group, one uint8 offset per kept value) at 32:64;
 
-each as a CUDA graph of back-to-back launches over enough weight copies to
+``--gemm 16,128,...`` instead times the prefill / batch > 1 GEMM
+(``nmsparse::gemm_packed``: gather + tcgen05 GEMM) against cuBLAS dense
+``F.linear`` for each token count and shape, with its roofline fraction
+(max of the HBM time and the tensor time of the sparse FLOPs).
+
+Each of the above runs as a CUDA graph of back-to-back launches over enough weight copies to
 span more than 3x the 126 MB L2 (so every launch streams from HBM), timed with
 CUDA events.  Achieved bandwidth = algorithmic bytes (kept values + mask
 offsets + vector + output; dense: the full matrix) / time, also as a fraction
@@ -45,6 +50,16 @@ from .nmsparse_op import unpack
 L2_BYTES = 126 * 2 ** 20
 SHAPES = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
 RATIOS = [(2, 4), (4, 8), (8, 16), (16, 32), (32, 64), (64, 128), (128, 256)]
+
+
+def _peak_tflops() -> tuple:
+    """Dense fp16/bf16 tensor peak (the burst cuBLAS figure), TFLOP/s."""
+    f = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def _peak_gbs() -> tuple:
@@ -249,6 +264,55 @@ def bench_dense_head(dev, reps: int, peak: float, V: int = 128256, K: int = 4096
     return r
 
 
+def bench_gemm(h: int, K: int, T: int, dev, reps: int, peak_gbs: float, peak_tf: float, M: int = 64) -> dict:
+    """Prefill / batch > 1: gather + tcgen05 GEMM (nms_gemm_packed_f16) for T
+    tokens against cuBLAS F.linear with a dense [h, K] fp16 weight.  Weight
+    copies rotate over > 3x L2.  Roofline time = max(algorithmic bytes / HBM
+    peak, sparse FLOPs (2 T h w) / tensor peak)."""
+    lib = _lib.lib()
+    packed, mi, w, nnz = make_sparse_device(K, h, M, 11, dev, std=0.02)
+    w_pad = packed.shape[1]
+    wbytes = packed.numel() * 2
+    nb = max(2, math.ceil(3 * L2_BYTES / wbytes) + 1)
+    packs = [packed] + [packed.clone() for _ in range(nb - 1)]
+    x = torch.randn(T, K, device=dev).to(torch.float16)
+    outs = [torch.empty(T, h, device=dev, dtype=torch.float16) for _ in range(nb)]
+    n = ctypes.c_int64(0)
+    _lib.check(lib.nms_gemm_workspace_bytes(T, w_pad, h, ctypes.byref(n)))
+    ws = torch.empty(n.value, dtype=torch.uint8, device=dev)
+
+    def ours(i):
+        def f(s):
+            _lib.check(lib.nms_gemm_packed_f16(x.data_ptr(), _lib.NMS_DTYPE_F16, packs[i].data_ptr(), mi.data_ptr(),
+                                               outs[i].data_ptr(), T, K, w, w_pad, h, nnz, M, ws.data_ptr(),
+                                               ws.numel(), s.cuda_stream), "nms_gemm_packed_f16")
+        return f
+
+    t_ours = _graph_time_us([ours(i) for i in range(nb)], dev, reps)
+    ref = x.float() @ masked_dense(unpack(packed, w), mi, K, M).float().t()
+    err = _max_rel(outs[0], ref)
+    del ref
+    dbytes = h * K * 2
+    nd = max(2, math.ceil(3 * L2_BYTES / dbytes) + 1)
+    Wd = [(torch.randn(h, K, device=dev) * 0.02).to(torch.float16) for _ in range(nd)]
+    od = [torch.empty(T, h, device=dev, dtype=torch.float16) for _ in range(nd)]
+    t_dense = _graph_time_us([(lambda i: lambda s: torch.matmul(x, Wd[i].t(), out=od[i]))(i) for i in range(nd)],
+                             dev, reps)
+    del Wd, od, packs
+    by = wbytes + mi.numel() + T * K * 2 + T * h * 2
+    flops = 2.0 * T * h * w
+    t_roof = max(by / peak_gbs / 1e3, flops / peak_tf / 1e6)
+    r = {"kind": "gemm", "shape": f"{h}x{K}", "nm": f"{nnz}:{M}", "T": T, "algorithmic_bytes": by,
+         "sparse_flops": flops, "us": round(t_ours, 3), "GBs": round(by / t_ours / 1e3, 1),
+         "TFLOPs": round(flops / t_ours / 1e6, 1), "roofline_us": round(t_roof, 3),
+         "frac": round(t_roof / t_ours, 3), "bound": "hbm" if by / peak_gbs / 1e3 >= flops / peak_tf / 1e6 else "tensor",
+         "max_rel": err, "cublas_dense_us": round(t_dense, 3),
+         "cublas_dense_TFLOPs": round(2.0 * T * h * K / t_dense / 1e6, 1),
+         "speedup_vs_cublas": round(t_dense / t_ours, 3)}
+    print(json.dumps(r), flush=True)
+    return r
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--shapes", default=",".join(f"{h}x{k}" for h, k in SHAPES))
@@ -256,12 +320,22 @@ def main(argv=None):
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--no-head", action="store_true")
     p.add_argument("--no-rowwise", action="store_true")
+    p.add_argument("--gemm", default="", help="token counts for the prefill GEMM, e.g. 16,128,512,2048 "
+                                              "(runs only the GEMM table)")
     args = p.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
     peak, src = _peak_gbs()
     shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s]
     ratios = [tuple(int(v) for v in r.split(":")) for r in args.ratios.split(",") if r]
     rows = []
+    if args.gemm:
+        tf, _ = _peak_tflops()
+        for T in [int(v) for v in args.gemm.split(",") if v]:
+            for h, K in shapes:
+                rows.append(bench_gemm(h, K, T, dev, args.reps, peak, tf))
+        print(json.dumps({"summary": True, "peak_GBs": peak, "peak_TFLOPs": tf, "peak_source": src,
+                          "rows": len(rows)}), flush=True)
+        return rows
     for h, K in shapes:
         rows += bench_shape(h, K, ratios, dev, args.reps, peak)
     if not args.no_rowwise:

@@ -11,7 +11,8 @@ Mirrors src/spmv/nmsparse_linear.py of the reference:
   reference constructor, attributes ``h, w, block_width, vec_width``,
   buffers ``mat_data`` and ``mat_index`` and forward rule (single token ->
   sparse GEMV, otherwise ``F.linear`` with the dense weight,
-  :55-68).  The difference is storage: ``mat_data`` holds the packed layout
+  :55-68).  Where the reference raises for want of a dense weight, a CUDA
+  input runs the sparse layer on the tensor cores (``nmsparse::gemm_packed``).  The difference is storage: ``mat_data`` holds the packed layout
   [h, w_pad] (row-major transpose, 16-byte aligned rows) that the sm_100a
   kernel streams; ``reference_mat_data()`` returns the reference [w, h]
   layout, and reference state dicts load unchanged (they are repacked).
@@ -174,6 +175,13 @@ class NmSparseLinear(nn.Module):
     def forward(self, x):
         if x.shape[-2] == 1:
             return torch.ops.nmsparse.gemv_packed(
+                x, self.mat_data, self.mat_index,
+                self.w, self.h, self.block_width, self.vec_width,
+            )
+        if self.weight is None and self._weight_cpu is None and x.is_cuda:
+            # No dense weight kept (the reference raises here, :57-61): run
+            # the sparse layer itself on the tensor cores.
+            return torch.ops.nmsparse.gemm_packed(
                 x, self.mat_data, self.mat_index,
                 self.w, self.h, self.block_width, self.vec_width,
             )

@@ -9,10 +9,13 @@ reference's shared-mask mode, whose layout this implements) and anything else
 raises ``ValueError`` like the reference's allow-list (src/spmv/nmsparse_op.py:20-22).
 
 Also registers ``nmsparse::gemv_packed`` for the re-laid-out weights that
-``NmSparseLinear`` stores (packed [h, w_pad] rows, see include/nmsparse_b200.h).
+``NmSparseLinear`` stores (packed [h, w_pad] rows, see include/nmsparse_b200.h),
+and ``nmsparse::gemm_packed``, the same product for any number of tokens
+(prefill / batch > 1) on the tensor cores.
 """
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
@@ -159,6 +162,68 @@ def gemv_packed(x: torch.Tensor, mat_packed: torch.Tensor, mat_index: torch.Tens
 
 
 @gemv_packed.register_fake
+def _(x, mat_packed, mat_index, w, h, block_width, vec_width):
+    return x.new_empty((*x.shape[:-1], int(h)))
+
+
+_GEMM_DTYPES = {torch.float16: _lib.NMS_DTYPE_F16, torch.bfloat16: _lib.NMS_DTYPE_BF16,
+                torch.float32: _lib.NMS_DTYPE_F32}
+
+
+def gemm_workspace_bytes(T: int, w_pad: int, h: int) -> int:
+    """Bytes of scratch nms_gemm_packed_f16 needs for T tokens (current device)."""
+    n = ctypes.c_int64(0)
+    _lib.check(_lib.lib().nms_gemm_workspace_bytes(int(T), int(w_pad), int(h), ctypes.byref(n)),
+               "nms_gemm_workspace_bytes")
+    return int(n.value)
+
+
+@torch.library.custom_op("nmsparse::gemm_packed", mutates_args=())
+def gemm_packed(x: torch.Tensor, mat_packed: torch.Tensor, mat_index: torch.Tensor,
+                w: int, h: int, block_width: int, vec_width: int) -> torch.Tensor:
+    """Shared-mask N:M product for any number of tokens (prefill / batch > 1)
+    on the packed layout: every row of ``x`` [..., K] goes through the same
+    sum as ``nmsparse::gemv`` (fp16 operands, fp32 accumulation, fp16
+    result cast back to ``x.dtype``), on the tensor cores.  The reference
+    has no multi-token sparse op; its linear falls back to a dense
+    F.linear (src/spmv/nmsparse_linear.py:55-68)."""
+    K = x.shape[-1]
+    x2d = x.reshape(-1, K)
+    if not x2d.is_contiguous():
+        x2d = x2d.contiguous()
+    T = x2d.shape[0]
+    if not x.is_cuda or not mat_packed.is_cuda or not mat_index.is_cuda:
+        raise ValueError("x, mat_packed, and mat_index must be CUDA tensors")
+    if x.dtype not in _GEMM_DTYPES:
+        raise TypeError(f"x must be float16, bfloat16 or float32, got {x.dtype}")
+    if mat_index.dtype != torch.uint8:
+        raise TypeError("mat_index must be uint8")
+    if mat_packed.dtype != torch.float16:
+        raise TypeError("mat_packed must be float16")
+    if mat_packed.ndim != 2 or mat_packed.shape[0] != h or not mat_packed.is_contiguous():
+        raise ValueError(f"mat_packed must be a contiguous [{h}, w_pad] tensor, got {tuple(mat_packed.shape)}")
+    if block_width <= 0 or w % block_width != 0:
+        raise ValueError(f"w={w} must be divisible by N={block_width}")
+    if tuple(mat_index.shape) != (w // block_width, block_width) or not mat_index.is_contiguous():
+        raise ValueError(f"mat_index must be a contiguous {(w // block_width, block_width)} tensor")
+    out = torch.empty((T, h), dtype=torch.float16, device=x.device)
+    if T == 0:
+        return out.to(dtype=x.dtype).reshape(*x.shape[:-1], int(h))
+    w_pad = mat_packed.shape[-1]
+    with torch.cuda.device(x.device):
+        ws = torch.empty(gemm_workspace_bytes(T, w_pad, h), dtype=torch.uint8, device=x.device)
+        _lib.check(
+            _lib.lib().nms_gemm_packed_f16(
+                x2d.data_ptr(), _GEMM_DTYPES[x.dtype], mat_packed.data_ptr(), mat_index.data_ptr(),
+                out.data_ptr(), int(T), int(K), int(w), int(w_pad), int(h), int(block_width),
+                int(vec_width), ws.data_ptr(), ws.numel(), _stream_ptr(x.device),
+            ),
+            "nms_gemm_packed_f16",
+        )
+    return out.to(dtype=x.dtype).reshape(*x.shape[:-1], int(h))
+
+
+@gemm_packed.register_fake
 def _(x, mat_packed, mat_index, w, h, block_width, vec_width):
     return x.new_empty((*x.shape[:-1], int(h)))
 

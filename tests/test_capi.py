@@ -136,3 +136,51 @@ def test_fake_kernel_shapes():
         mi = torch.empty(16, 16, dtype=torch.uint8)
         y = torch.ops.nmsparse.gemv(x, md, mi, 256, 384, 16, 32)
         assert tuple(y.shape) == (1, 1, 384)
+
+
+def _call_gemm(**kw):
+    a = dict(x=256, dt=_lib.NMS_DTYPE_F16, packed=256, mi=256, out=256, T=128, K=4096, w=2048, w_pad=2048, h=4096,
+             bw=32, vw=64, ws=256, wsb=1 << 30)
+    a.update(kw)
+    return _lib.lib().nms_gemm_packed_f16(a["x"], a["dt"], a["packed"], a["mi"], a["out"], a["T"], a["K"], a["w"],
+                                          a["w_pad"], a["h"], a["bw"], a["vw"], a["ws"], a["wsb"], None)
+
+
+@pytest.mark.parametrize(
+    "kw,status,msg",
+    [
+        (dict(x=None), _lib.NMS_ERR_VALUE, "null pointer"),
+        (dict(ws=None), _lib.NMS_ERR_VALUE, "null pointer"),
+        (dict(dt=7), _lib.NMS_ERR_TYPE, "x_dtype=7"),
+        (dict(T=0), _lib.NMS_ERR_VALUE, "T=0"),
+        (dict(K=4000), _lib.NMS_ERR_VALUE, "K=4000"),
+        (dict(w=2047), _lib.NMS_ERR_VALUE, "divisible by N"),
+        (dict(w_pad=2050), _lib.NMS_ERR_VALUE, "w_pad=2050"),
+        (dict(bw=64, vw=32), _lib.NMS_ERR_VALUE, "N <= M"),
+        (dict(packed=264), _lib.NMS_ERR_VALUE, "16-byte aligned"),
+        (dict(ws=272), _lib.NMS_ERR_VALUE, "256-byte aligned"),
+        (dict(x=257), _lib.NMS_ERR_VALUE, "element size"),
+    ],
+)
+def test_gemm_argument_validation(kw, status, msg):
+    """The prefill GEMM validates every argument before touching the device."""
+    rc = _call_gemm(**kw)
+    assert rc == status
+    assert msg in _lib.lib().nms_last_error().decode()
+
+
+def test_gemm_op_rejects_cpu_tensors():
+    from spmv_decode_b200 import nmsparse_op  # noqa: F401
+
+    x = torch.randn(4, 256, dtype=torch.float16)
+    packed = torch.zeros(128, 128, dtype=torch.float16)
+    mi = torch.zeros(8, 16, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        torch.ops.nmsparse.gemm_packed(x, packed, mi, 128, 128, 16, 32)
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        y = torch.ops.nmsparse.gemm_packed(torch.empty(3, 5, 256, dtype=torch.bfloat16),
+                                           torch.empty(384, 128, dtype=torch.float16),
+                                           torch.empty(8, 16, dtype=torch.uint8), 128, 384, 16, 32)
+        assert tuple(y.shape) == (3, 5, 384) and y.dtype == torch.bfloat16

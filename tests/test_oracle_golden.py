@@ -153,3 +153,19 @@ def test_shared_mask_topk_packer():
     dense = O.masked_dense(md, mi, K, m)
     cols = O.gather_columns(mi, m)
     np.testing.assert_array_equal(dense[:, cols], W[:, cols])
+
+
+def test_gemm_oracle_is_the_gemv_oracle_row_by_row():
+    """gemm_fp32 (multi-token oracle) equals gemv_fp32 on every token."""
+    from oracle import nm_oracle as O2
+
+    rng = np.random.default_rng(3)
+    K, m, n, h, T = 512, 16, 8, 96, 5
+    G = K // m
+    mi = np.stack([np.sort(rng.permutation(m)[:n]) for _ in range(G)]).astype(np.uint8)
+    md = (rng.standard_normal((G * n, h)) * 0.05).astype(np.float16)
+    X = rng.standard_normal((T, K)).astype(np.float16)
+    Y = O2.gemm_fp32(X, md, mi, K, m)
+    assert Y.shape == (T, h) and Y.dtype == np.float32
+    for t in range(T):
+        np.testing.assert_allclose(Y[t], O2.gemv_fp32(X[t], md, mi, K, m), rtol=1e-5, atol=1e-6)
