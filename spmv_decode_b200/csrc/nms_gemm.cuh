@@ -21,13 +21,13 @@
 //                     tcgen05.ld.  Both operands are K-major: row r of the
 //                     packed matrix is A's row, token t of xc is B's row.
 //
-// Split-K (only when even 32-token tiles leave SMs idle): the S k-splits of
-// one tile run as one thread-block cluster.  Each CTA stages its fp32
-// partial tile in its own shared memory; after a cluster barrier, CTA r sums
-// columns [r*BN/S, (r+1)*BN/S) of all S partials over distributed shared
-// memory in split order (so the result does not depend on timing) and writes
-// them; a second cluster barrier keeps every partial alive until all reads
-// are done.
+// Split-K (when the tiles alone leave SMs idle): the S k-splits of one tile
+// run as one thread-block cluster.  After a cluster barrier (every main loop
+// done, so the shared-memory rings are free), each CTA pushes its fp32
+// partial, 16 columns at a time, into the shared memory of the CTA that owns
+// those columns (16-byte remote stores over distributed shared memory);
+// after a second barrier each owner sums its columns over the S partials in
+// split order (so the result does not depend on timing) and writes them.
 //
 // Every mbarrier wait is bounded (kGemmWaitNs); a wait that runs out records
 // kDevMmaTimeout in the device error word and the CTA finishes without
@@ -44,7 +44,8 @@
 namespace nms {
 
 constexpr int kGemmBM = 128;          // rows of h per tile (UMMA M)
-constexpr int kGemmBK = 64;           // compressed columns per stage: one 128-byte swizzle row
+constexpr int kGemmBK = 64;           // compressed columns per swizzle atom: one 128-byte row
+constexpr int kGemmMaxAtoms = 2;      // atoms per pipeline stage
 constexpr int kGemmThreads = 128;     // 4 warps: TMA producer, MMA issuer, TMEM owner, all epilogue
 constexpr int kGemmMaxStages = 8;
 constexpr int kGemmMaxBN = 256;       // UMMA N limit and TMA box limit
@@ -55,7 +56,8 @@ struct GemmParams {
   __half* out;           // [T, h] fp16
   int32_t T, h;
   int32_t bn;            // tokens per tile (multiple of 16, <= 256)
-  int32_t kblocks;       // w_pad / 64
+  int32_t atoms;         // 64-column atoms per stage (1 or 2)
+  int32_t kblocks;       // stages covering w_pad: ceil(w_pad / (64 * atoms))
   int32_t splits;        // k-splits per tile (<= kblocks, <= 8): the cluster size along z
   int32_t stages;        // shared-memory ring depth
   uint32_t idesc;        // tcgen05 instruction descriptor
@@ -74,19 +76,28 @@ template <typename TX>
 __global__ void __launch_bounds__(256) gather_xc_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ idx,
                                                         __half* __restrict__ xc, int32_t T, int32_t K, int32_t w,
                                                         int32_t w_pad, int32_t n, int32_t m) {
+  // The GEMM that follows is launched as a programmatic dependent: let it
+  // start its prologue and weight loads now (it waits for this grid before
+  // it reads xc).
+  grid_dep_launch_dependents();
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int32_t chunks = w_pad >> 3;
   if (gid >= (int64_t)T * chunks) return;
   const int32_t t = (int32_t)(gid / chunks);
   const int32_t j0 = (int32_t)(gid - (int64_t)t * chunks) * 8;
   const TX* xr = x + (int64_t)t * K;
+  int32_t g = j0 / n, i = j0 - g * n;  // group and slot of j0, then stepped
   __align__(16) __half v[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int32_t j = j0 + q;
     float f = 0.f;
-    if (j < w) f = to_f32(xr[(j / n) * m + idx[j]]);
+    if (j < w) f = to_f32(xr[g * m + idx[j]]);
     v[q] = __float2half_rn(f);
+    if (++i == n) {
+      i = 0;
+      ++g;
+    }
   }
   *reinterpret_cast<uint4*>(xc + (int64_t)t * w_pad + j0) = *reinterpret_cast<const uint4*>(v);
 }
@@ -175,6 +186,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Shared-window address of `local` (an address in this CTA's shared memory)
+// in cluster rank `rank`'s shared memory.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+  return remote;
+}
+
+__device__ __forceinline__ void st_dsmem_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
@@ -210,8 +234,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const uint32_t raw = smem_u32(gemm_smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t a_bytes = kGemmBM * 128u, b_bytes = (uint32_t)p.bn * 128u;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
+  // Stage s: atoms x A tile [128 rows][128 B], then atoms x B tile [bn][128 B].
+  const uint32_t a_atom = kGemmBM * 128u, b_atom = (uint32_t)p.bn * 128u;
+  const uint32_t a_bytes = a_atom * (uint32_t)p.atoms;
+  const uint32_t stage_bytes = a_bytes + b_atom * (uint32_t)p.atoms;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -232,41 +258,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // TMA producer.
-    int i = 0;
+    // TMA producer.  A stage past w_pad (odd atom count) reads the zero fill.
+    // The first ring's weight tiles are requested before the gather grid has
+    // finished (this grid is its programmatic dependent); xc tiles only after.
+    int i = 0, s = 0;
+    uint32_t ph = 0;
+    const int npre = nk < p.stages ? nk : p.stages;
+    for (; i < npre; ++i) {
+      const uint32_t sa = base + (uint32_t)i * stage_bytes;
+      const int32_t kx = (kb0 + i) * kGemmBK * p.atoms;
+      mbar_arrive_expect_tx(&full_bar[i], stage_bytes);
+      for (int a = 0; a < p.atoms; ++a)
+        tma_load_2d(sa + (uint32_t)a * a_atom, &tm_a, kx + a * kGemmBK, m0, smem_u32(&full_bar[i]));
+    }
+    grid_dep_wait();
+    for (int j = 0; j < npre; ++j) {
+      const uint32_t sb = base + (uint32_t)j * stage_bytes + a_bytes;
+      const int32_t kx = (kb0 + j) * kGemmBK * p.atoms;
+      for (int a = 0; a < p.atoms; ++a)
+        tma_load_2d(sb + (uint32_t)a * b_atom, &tm_b, kx + a * kGemmBK, n0, smem_u32(&full_bar[j]));
+    }
+    if (npre == p.stages) {
+      s = 0;
+      ph = 1u;
+    } else {
+      s = npre;
+    }
     for (; i < nk; ++i) {
-      const int s = i % p.stages;
-      const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
       if (!gemm_wait(&empty_bar[s], ph ^ 1u)) {
         atomicExch(&s_abort, 1);
         break;
       }
-      if (*(volatile int32_t*)&s_abort) break;
       const uint32_t sa = base + (uint32_t)s * stage_bytes;
-      const int32_t kx = (kb0 + i) * kGemmBK;
+      const uint32_t bar = smem_u32(&full_bar[s]);
+      const int32_t kx = (kb0 + i) * kGemmBK * p.atoms;
       mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
-      tma_load_2d(sa, &tm_a, kx, m0, smem_u32(&full_bar[s]));
-      tma_load_2d(sa + a_bytes, &tm_b, kx, n0, smem_u32(&full_bar[s]));
+      for (int a = 0; a < p.atoms; ++a) {
+        tma_load_2d(sa + (uint32_t)a * a_atom, &tm_a, kx + a * kGemmBK, m0, bar);
+        tma_load_2d(sa + a_bytes + (uint32_t)a * b_atom, &tm_b, kx + a * kGemmBK, n0, bar);
+      }
+      if (++s == p.stages) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
     s_issued = i;
   } else if (warp == 1 && lane == 0) {
-    // MMA issuer: 4 MMAs (K = 16 each) per 64-column stage; advancing K by 16
+    // MMA issuer: 4 MMAs (K = 16 each) per 64-column atom; advancing K by 16
     // fp16 inside the 128-byte swizzle row is +32 bytes on the start address.
-    int i = 0;
+    int i = 0, s = 0;
+    uint32_t ph = 0;
     for (; i < nk; ++i) {
-      const int s = i % p.stages;
-      const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
       if (!gemm_wait(&full_bar[s], ph)) {
         atomicExch(&s_abort, 1);
         break;
       }
       tc_fence_after();
       const uint32_t sa = base + (uint32_t)s * stage_bytes;
-      const uint64_t da = umma_desc_k_sw128(sa), db = umma_desc_k_sw128(sa + a_bytes);
+      for (int a = 0; a < p.atoms; ++a) {
+        const uint64_t da = umma_desc_k_sw128(sa + (uint32_t)a * a_atom);
+        const uint64_t db = umma_desc_k_sw128(sa + a_bytes + (uint32_t)a * b_atom);
 #pragma unroll
-      for (int kk = 0; kk < kGemmBK / 16; ++kk)
-        umma_f16(tmem, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), p.idesc, (i | kk) != 0 ? 1u : 0u);
+        for (int kk = 0; kk < kGemmBK / 16; ++kk)
+          umma_f16(tmem, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), p.idesc, (i | a | kk) != 0 ? 1u : 0u);
+      }
       umma_commit(smem_u32(&empty_bar[s]));
+      if (++s == p.stages) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
     s_consumed = i;
     umma_commit(smem_u32(&accum_bar));
@@ -278,27 +338,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const int row = warp * 32 + lane;
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-  __half* out_s = reinterpret_cast<__half*>(gemm_smem_raw + (base - raw));
   const int nchunks = p.bn >> 4;
+  // Token range [t_begin, t_begin + t_count) of the tile this CTA writes,
+  // staged as fp16 rows out_s[t][128 + 8 pad] before coalesced stores.
+  __half* out_s = reinterpret_cast<__half*>(gemm_smem_raw + (base - raw));
+  int t_begin = 0, t_count = p.bn;
   if (p.splits > 1) {
-    // Partial tile -> own shared memory, column-major [bn][128] fp32.
-    float* part_s = reinterpret_cast<float*>(gemm_smem_raw + (base - raw));
+    // 16-column chunks of the tile are owned by cluster ranks in blocks of
+    // cpr.  Every rank pushes each chunk of its partial into the owner's
+    // receive buffer recv[split][128 rows][cpr * 16 columns + 4 pad] (four
+    // 16-byte remote stores per thread and chunk); the owner then sums its
+    // columns over the splits in split order.
+    const int S = p.splits, r = (int)cluster_ctarank();
+    const int cpr = (nchunks + S - 1) / S;
+    const uint32_t pitch = (uint32_t)cpr * 16u + 4u;  // floats per receive row
+    cluster_sync_all();  // every rank is past its main loop: the rings are free
     for (int c = 0; c < nchunks; ++c) {
       float v[16];
       tmem_ld16(trow + (uint32_t)(c * 16), v);
+      const int q = c / cpr, lc = c - q * cpr;
+      const uint32_t dst =
+          dsmem_addr(base, (uint32_t)q) + (((uint32_t)r * kGemmBM + (uint32_t)row) * pitch + (uint32_t)lc * 16u) * 4u;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) part_s[(c * 16 + j) * kGemmBM + row] = v[j];
+      for (int e = 0; e < 4; ++e) st_dsmem_v4(dst + 16u * e, v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
     }
-    cluster_sync_all();
-    const int r = (int)cluster_ctarank();
-    const int c0 = p.bn * r / p.splits, c1 = p.bn * (r + 1) / p.splits;
-    const bool row_ok = acc_ok && m0 + row < p.h;
-    for (int col = c0; col < c1; ++col) {
-      float acc = 0.f;
-      for (int s = 0; s < p.splits; ++s) acc += ld_dsmem_f32(part_s + col * kGemmBM + row, (uint32_t)s);
-      if (row_ok && n0 + col < p.T) p.out[(int64_t)(n0 + col) * p.h + m0 + row] = __float2half_rn(acc);
+    cluster_sync_all();  // all pushes have landed
+    const int c_first = r * cpr;
+    const int c_end = min(nchunks, c_first + cpr);
+    t_begin = c_first * 16;
+    t_count = c_end > c_first ? (c_end - c_first) * 16 : 0;
+    const float* recv = reinterpret_cast<const float*>(gemm_smem_raw + (base - raw));
+    out_s = reinterpret_cast<__half*>(gemm_smem_raw + (base - raw) + (size_t)S * kGemmBM * pitch * 4);
+    for (int lc = 0; lc * 16 < t_count; ++lc) {
+      float acc[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+      for (int sp = 0; sp < S; ++sp) {
+        const float4* src = reinterpret_cast<const float4*>(recv + ((size_t)sp * kGemmBM + row) * pitch + lc * 16);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 f = src[e];
+          acc[4 * e] += f.x;
+          acc[4 * e + 1] += f.y;
+          acc[4 * e + 2] += f.z;
+          acc[4 * e + 3] += f.w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out_s[(lc * 16 + j) * kGemmOutPitch + row] = __float2half_rn(acc[j]);
     }
-    cluster_sync_all();
   } else {
     for (int c = 0; c < nchunks; ++c) {
       float v[16];
@@ -308,13 +396,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
   __syncthreads();
-  if (p.splits == 1 && acc_ok) {
-    const int rows_valid = min(p.bn, p.T - n0);
+  if (acc_ok) {
+    const int rows_valid = min(t_count, p.T - n0 - t_begin);
     const int cols_valid = min(kGemmBM, p.h - m0);
-    for (int q = threadIdx.x; q < p.bn * (kGemmBM / 8); q += kGemmThreads) {
+    for (int q = threadIdx.x; q < t_count * (kGemmBM / 8); q += kGemmThreads) {
       const int t = q >> 4, c8 = (q & 15) * 8;
       if (t >= rows_valid || c8 >= cols_valid) continue;
-      __half* dst = p.out + (int64_t)(n0 + t) * p.h + m0 + c8;
+      __half* dst = p.out + (int64_t)(n0 + t_begin + t) * p.h + m0 + c8;
       const __half* src = out_s + t * kGemmOutPitch + c8;
       if (p.vec_out && c8 + 8 <= cols_valid) {
         *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);

@@ -494,7 +494,7 @@ int noalloc_scratch(unsigned char** out) {
 // Prefill GEMM (nms_gemm.cuh): tile plan, workspace layout, tensor maps.
 // ---------------------------------------------------------------------------
 struct GemmPlan {
-  int32_t m_tiles = 0, n_tiles = 0, bn = 0, splits = 1, stages = 0, kblocks = 0;
+  int32_t m_tiles = 0, n_tiles = 0, bn = 0, splits = 1, stages = 0, atoms = 1, kblocks = 0;
   size_t smem = 0;
   int64_t total = 0;  // workspace bytes: xc [T, w_pad] fp16
 };
@@ -502,34 +502,87 @@ struct GemmPlan {
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
 // Tokens are split into ceil(T / 256) equal tiles (UMMA N <= 256, a multiple
-// of 16); rows of h into 128-row tiles.  While the tiles fill less than half
-// the SMs, the token tiles are halved (down to 32 tokens: the weight tile is
-// then re-read by the CTAs of one row block, mostly from L2).  If the tiles
-// still leave SMs idle, the compressed width is split too: at most 8 ways (the
-// portable cluster size), at least one 64-column stage per split.  The ring
-// takes as many stages (<= 8) as shared memory holds.
+// of 16); rows of h into 128-row tiles.  If the tiles leave SMs idle, the
+// compressed width is split first (a cluster of up to 8 CTAs per tile: every
+// weight byte is still loaded once); only if that still fills less than half
+// the SMs are the token tiles halved (down to 32 tokens: each halving makes
+// one more CTA load the same weight tile).  Token tiles of <= 64 take two
+// 64-column atoms per stage, so one barrier round trip of the producer and
+// MMA threads feeds 8 MMAs instead of 4.  The ring takes as many stages
+// (<= 8) as shared memory holds.
+// Clusters of `size` CTAs (one tile's k-splits) that can be resident at
+// once with `smem` bytes of dynamic shared memory each; clusters are placed
+// inside one GPC, so some sizes leave SMs unusable.  Cached per device.
+int gemm_max_clusters(int size, size_t smem, int* out) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, int>, std::pair<size_t, int>>> cache;  // ((dev, size), (smem, n))
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto& c : cache)
+    if (c.first.first == dev && c.first.second == size && c.second.first == smem) {
+      *out = c.second.second;
+      return NMS_OK;
+    }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(1, 1, (unsigned)size);
+  cfg.blockDim = dim3(nms::kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeClusterDimension;
+  a.val.clusterDim.x = 1;
+  a.val.clusterDim.y = 1;
+  a.val.clusterDim.z = (unsigned)size;
+  cfg.attrs = &a;
+  cfg.numAttrs = 1;
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, (const void*)nms::gemm_nm_kernel, &cfg);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaOccupancyMaxActiveClusters");
+  cache.push_back({{dev, size}, {smem, n}});
+  *out = n;
+  return NMS_OK;
+}
+
 int gemm_plan(int64_t T, int64_t w_pad, int64_t h, int num_sms, size_t smem_max, GemmPlan* g) {
   g->n_tiles = (int32_t)((T + nms::kGemmMaxBN - 1) / nms::kGemmMaxBN);
   g->bn = (int32_t)std::max<int64_t>(16, round_up((T + g->n_tiles - 1) / g->n_tiles, 16));
   g->m_tiles = (int32_t)((h + nms::kGemmBM - 1) / nms::kGemmBM);
-  g->kblocks = (int32_t)(w_pad / nms::kGemmBK);
-  while (g->bn >= 64 && (int64_t)g->m_tiles * g->n_tiles * 2 <= num_sms) {
+  int64_t tiles = 0;
+  auto fill = [&]() {
+    tiles = (int64_t)g->m_tiles * g->n_tiles;
+    g->splits = tiles < num_sms ? (int32_t)std::min<int64_t>(8, num_sms / tiles) : 1;
+  };
+  fill();
+  while (g->bn >= 64 && tiles * g->splits * 2 <= num_sms) {
     g->bn = (int32_t)round_up(g->bn / 2, 16);
     g->n_tiles = (int32_t)((T + g->bn - 1) / g->bn);
+    fill();
   }
-  const int64_t tiles = (int64_t)g->m_tiles * g->n_tiles;
-  g->splits = 1;
-  if (tiles < num_sms) {
-    g->splits = (int32_t)std::min<int64_t>({(int64_t)num_sms / tiles, (int64_t)g->kblocks, 8});
-    if (g->splits < 1) g->splits = 1;
-  }
-  const size_t stage = (size_t)nms::kGemmBM * 128 + (size_t)g->bn * 128;
+  g->atoms = g->bn <= 64 ? 2 : 1;
+  g->kblocks = (int32_t)((w_pad / nms::kGemmBK + g->atoms - 1) / g->atoms);
+  if (g->splits > g->kblocks) g->splits = g->kblocks;
+  if (g->splits < 1) g->splits = 1;
+  const size_t stage = ((size_t)nms::kGemmBM * 128 + (size_t)g->bn * 128) * g->atoms;
   const size_t avail = smem_max > 1024 ? smem_max - 1024 : 0;
   g->stages = (int32_t)std::min<size_t>(nms::kGemmMaxStages, avail / stage);
   if (g->stages < 2) return fail(NMS_ERR_NOT_IMPLEMENTED, "gemm: %zu B of shared memory holds fewer than 2 stages", smem_max);
   g->smem = 1024 + (size_t)g->stages * stage;
-  // Epilogue staging reuses the ring: fp16 output rows, or the fp32 partial.
-  const size_t staging = g->splits > 1 ? (size_t)g->bn * nms::kGemmBM * 4 : (size_t)g->bn * nms::kGemmOutPitch * 2;
+  // Keep every tile's cluster resident in one wave: shrink the split count
+  // until the GPCs hold `tiles` clusters of that size.
+  while (g->splits > 1) {
+    int fit = 0;
+    int rc = gemm_max_clusters(g->splits, g->smem, &fit);
+    if (rc) return rc;
+    if (fit >= tiles) break;
+    --g->splits;
+  }
+  // Epilogue staging reuses the ring: fp16 output rows, after the split-K
+  // receive buffer (splits x 128 rows x (owned columns + 4) fp32) when split.
+  const int64_t ncl = (g->bn / 16 + g->splits - 1) / g->splits * 16;
+  const size_t staging = g->splits > 1 ? (size_t)g->splits * nms::kGemmBM * (ncl + 4) * 4 + (size_t)ncl * nms::kGemmOutPitch * 2
+                                       : (size_t)g->bn * nms::kGemmOutPitch * 2;
   if (staging > (size_t)g->stages * stage)
     return fail(NMS_ERR_NOT_IMPLEMENTED, "gemm: epilogue staging of %zu B exceeds the ring", staging);
   g->total = round_up(T * w_pad * 2, 256);
@@ -1238,6 +1291,7 @@ int nms_gemm_packed_f16(const void* x, int32_t x_dtype, const void* packed, cons
   p.T = (int32_t)T;
   p.h = (int32_t)h;
   p.bn = g.bn;
+  p.atoms = g.atoms;
   p.kblocks = g.kblocks;
   p.splits = g.splits;
   p.stages = g.stages;
@@ -1251,13 +1305,17 @@ int nms_gemm_packed_f16(const void* x, int32_t x_dtype, const void* packed, cons
   cfg.blockDim = dim3(nms::kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = g.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = (unsigned)g.splits;  // the k-splits of one tile form a cluster
+  // Programmatic dependent of the gather: the prologue and the first weight
+  // tiles overlap it; xc is read only after griddepcontrol.wait.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, nms::gemm_nm_kernel, tm_a, tm_b, p);
   if (e != cudaSuccess) return fail_cuda(e, "gemm_nm_kernel launch");
   return NMS_OK;
