@@ -31,10 +31,11 @@ from typing import Callable, List, Optional
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _lib
 from .model import Transformer, precompute_rope_table
-from .nmsparse_linear import NmSparseLinear
+from .nmsparse_linear import NmSparseLinear, sparse_prefill
 
 ARGMAX_CAPACITY = 2048
 
@@ -347,6 +348,51 @@ class DecodeEngine:
             with torch.cuda.stream(stream):
                 self.head_hook(advance)
 
+    def prefill(self, tokens, start_pos: int = 0) -> torch.Tensor:
+        """Batched prefill: run ``tokens`` at positions ``start_pos ..`` through
+        the model's own layers in one pass -- every N:M projection as one
+        tensor-core GEMM over all the tokens (``nmsparse::gemm_packed``, the
+        same sparse weights the decode steps use), attention by
+        ``F.scaled_dot_product_attention`` under the causal mask -- writing
+        K/V straight into this engine's caches.  Leaves ``pos`` at the next
+        position and ``token_in`` at the greedy next token, so a decode step
+        continues from there.  Returns the last token's logits (fp16 [vocab]).
+
+        The reference prefills through a dense ``F.linear`` with the unpruned
+        weights (src/spmv/nmsparse_linear.py:55-68) or token by token through
+        the decode path (NM_DECODE_ONLY=1); this is the sparse batched form."""
+        if self.tp_size != 1:
+            raise NotImplementedError("batched prefill runs on one GPU; a tensor-parallel engine takes the prompt "
+                                      "through its decode step")
+        toks = torch.as_tensor(list(tokens), dtype=torch.int64).to(self.device)
+        T = int(toks.numel())
+        if T == 0:
+            raise ValueError("prefill needs at least one token")
+        if start_pos < 0 or start_pos + T > self.max_seq_length:
+            raise ValueError(f"positions [{start_pos}, {start_pos + T}) outside the cache of {self.max_seq_length}")
+        m = self.model
+        saved = [blk.attn.kv_cache for blk in m.layers]
+        try:
+            for li, blk in enumerate(m.layers):
+                blk.attn.kv_cache = _CacheView(self.k_cache[li:li + 1], self.v_cache[li:li + 1])
+            with torch.no_grad(), torch.cuda.device(self.device), sparse_prefill():
+                input_pos = torch.arange(start_pos, start_pos + T, device=self.device)
+                rope = self.rope[input_pos]
+                x = m.tok_embeddings(toks.view(1, T))
+                for blk in m.layers:
+                    x = blk(x, input_pos, rope)
+                x = m.norm(x[:, -1:])
+                logits = F.linear(x, m.output_weight).view(-1)
+                nxt = torch.argmax(logits).view(1)
+                self.pos.fill_(start_pos + T)
+                self.token_in.copy_(nxt)
+                if start_pos + T - 1 < self.history.numel():
+                    self.history[start_pos + T - 1: start_pos + T].copy_(nxt)
+        finally:
+            for blk, kv in zip(m.layers, saved):
+                blk.attn.kv_cache = kv
+        return logits
+
     def reset(self) -> None:
         self.k_cache.zero_()
         self.v_cache.zero_()
@@ -436,6 +482,20 @@ class _HeadLinear:
 
     def __init__(self, weight: torch.Tensor):
         self.weight = weight
+
+
+class _CacheView(nn.Module):
+    """KV-cache update onto one layer of the engine's caches ([1, Hkv, S, D]
+    views), for the model's eager attention during a batched prefill."""
+
+    def __init__(self, k: torch.Tensor, v: torch.Tensor):
+        super().__init__()
+        self.k, self.v = k, v
+
+    def update(self, input_pos, k_val, v_val):
+        self.k[:, :, input_pos] = k_val
+        self.v[:, :, input_pos] = v_val
+        return self.k, self.v
 
 
 def smoke_step(dev: torch.device) -> None:

@@ -8,7 +8,8 @@
   the next input token and advances the position on the device, so the loop
   needs no host synchronisation.  Prompt tokens are fed one per step through
   the same decode path (prefill in decode-only mode, which every reference
-  benchmark uses: NM_DECODE_ONLY=1).
+  benchmark uses: NM_DECODE_ONLY=1), or with ``batched_prefill=True`` all
+  at once through ``DecodeEngine.prefill`` (sparse tensor-core GEMMs).
 * ``build_model`` -- a Transformer for a named configuration with N:M
   sparse (or dense) linears; ``init="reference"`` reproduces the reference
   packer bit for bit, ``init="device"`` draws the same distributions on the
@@ -68,8 +69,17 @@ class GraphDecoder:
         return toks, (torch.stack(logits) if keep_logits else None)
 
 
-def generate(engine: DecodeEngine, prompt: Sequence[int], max_new_tokens: int) -> List[int]:
-    """Greedy generation through a captured decode step (generate.py:176-247)."""
+def generate(engine: DecodeEngine, prompt: Sequence[int], max_new_tokens: int, *,
+             batched_prefill: bool = False) -> List[int]:
+    """Greedy generation through a captured decode step (generate.py:176-247).
+
+    ``batched_prefill=True`` first runs all prompt tokens but the last through
+    ``engine.prefill`` (one sparse tensor-core GEMM per projection for the
+    whole prompt) instead of one decode step per prompt token."""
+    prompt = list(prompt)
+    if batched_prefill and len(prompt) > 1:
+        engine.prefill(prompt[:-1])
+        return GraphDecoder(engine).run(prompt[-1:], max_new_tokens, start_pos=len(prompt) - 1)[0]
     return GraphDecoder(engine).run(prompt, max_new_tokens)[0]
 
 

@@ -24,6 +24,7 @@ reference meaning (:7-8).
 """
 from __future__ import annotations
 
+import contextlib
 import os
 
 import torch
@@ -37,6 +38,24 @@ DECODE_ONLY = os.environ.get("NM_DECODE_ONLY", "0") == "1"
 WEIGHT_CPU = os.environ.get("NM_WEIGHT_CPU", "0") == "1" or DECODE_ONLY
 
 LAYOUT_PACKED = 1
+
+_SPARSE_PREFILL = False
+
+
+@contextlib.contextmanager
+def sparse_prefill(enabled: bool = True):
+    """Inside the block, multi-token CUDA input to NmSparseLinear runs the
+    sparse tensor-core GEMM even when a dense weight is kept -- the same
+    weights single-token decode uses (the decode engine's batched prefill).
+    Outside it the reference rule holds: dense ``F.linear`` when a dense
+    weight is kept (src/spmv/nmsparse_linear.py:55-68)."""
+    global _SPARSE_PREFILL
+    old = _SPARSE_PREFILL
+    _SPARSE_PREFILL = bool(enabled)
+    try:
+        yield
+    finally:
+        _SPARSE_PREFILL = old
 
 
 def make_sparse(K: int, N: int, M: int, seed: int, device="cpu"):
@@ -178,9 +197,9 @@ class NmSparseLinear(nn.Module):
                 x, self.mat_data, self.mat_index,
                 self.w, self.h, self.block_width, self.vec_width,
             )
-        if self.weight is None and self._weight_cpu is None and x.is_cuda:
-            # No dense weight kept (the reference raises here, :57-61): run
-            # the sparse layer itself on the tensor cores.
+        if x.is_cuda and (_SPARSE_PREFILL or (self.weight is None and self._weight_cpu is None)):
+            # No dense weight kept (the reference raises here, :57-61), or
+            # inside sparse_prefill(): the sparse layer on the tensor cores.
             return torch.ops.nmsparse.gemm_packed(
                 x, self.mat_data, self.mat_index,
                 self.w, self.h, self.block_width, self.vec_width,

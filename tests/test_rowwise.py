@@ -50,3 +50,4 @@ def test_rowwise_config1_round_trip():
     lo_kept = np.where(keep, A, np.inf).min(axis=2)
     hi_drop = np.where(~keep, A, -np.inf).max(axis=2)
     assert (lo_kept >= hi_drop).all()
+
