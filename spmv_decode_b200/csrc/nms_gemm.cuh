@@ -213,8 +213,9 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------
-// The GEMM.  grid = (m tiles, n tiles, splits), 128 threads, dynamic shared
-// memory = 1 KB alignment slack + stages x (16 KB A + bn x 128 B B).
+// The GEMM.  grid = (m tiles, n tiles, splits) with clusters of (1, 1,
+// splits), 128 threads, dynamic shared memory = 1 KB alignment slack +
+// stages x atoms x (16 KB A + bn x 128 B B).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_nm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
