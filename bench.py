@@ -206,12 +206,13 @@ def run_reference_arm(args, world: int, rank: int) -> None:
     threads = os.cpu_count() or 1
     # Each "step" is one sampled token; keep the run bounded.
     steps = max(1, min(args.steps, 5))
+    warm = max(3, min(args.warmup, 5))
     r = cpu_decode_sample(cfg, nm, args.ctx, sample_layers=args.cpu_layers, steps=steps, threads=threads,
-                          seed=args.seed)
+                          seed=args.seed, warmup=warm)
     v = r["ms_per_token"]
     line = {
         "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": steps,
-        "warmup": 1, "ms_per_step": round(v, 3), "higher_is_better": False, "scaling": "strong",
+        "warmup": warm, "ms_per_step": round(v, 3), "higher_is_better": False, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16 (torch CPU F.linear)", "data": "synthetic random-init weights",
         "impl": "reference",
         "config": {"workload": workload_name(args),
@@ -424,7 +425,7 @@ def main():
         from oracle.decode_oracle import cpu_decode_sample
 
         r = cpu_decode_sample(cfg, nm, args.ctx, sample_layers=args.cpu_layers, steps=3,
-                              threads=os.cpu_count(), seed=args.seed)
+                              threads=os.cpu_count(), seed=args.seed, warmup=3)
         cpu = {"value": round(r["ms_per_token"], 3), "unit": UNIT, "cores": r["threads"], "kind": "port",
                "sample": r["sample"]}
 

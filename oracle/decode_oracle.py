@@ -297,7 +297,7 @@ def _masked_random(rows: int, K: int, m: Optional[int], std: float, gen: torch.G
 
 
 def cpu_decode_sample(config, nm: Optional[tuple], ctx: int, sample_layers: int = 2, steps: int = 3,
-                      threads: Optional[int] = None, seed: int = 0) -> dict:
+                      threads: Optional[int] = None, seed: int = 0, warmup: int = 1) -> dict:
     """Time the reference's torch CPU decode path on a bounded sample of a
     workload: ``sample_layers`` decoder layers of the configuration's shapes
     plus the full output head, dense masked fp16 weights multiplied with
@@ -332,7 +332,9 @@ def cpu_decode_sample(config, nm: Optional[tuple], ctx: int, sample_layers: int 
         kc.normal_(0, 0.02, generator=gen)
         vc.normal_(0, 0.02, generator=gen)
     x = torch.randn(c.dim, generator=gen).to(torch.float16)
-    om.step(123, ctx)  # warm-up
+    for _ in range(max(1, warmup)):  # untimed warm-up steps
+        om.step(123, ctx)
+        om._linear(om.head, x)
     t_step, t_head = [], []
     for i in range(steps):
         t0 = time.perf_counter()
