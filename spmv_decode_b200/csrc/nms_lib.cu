@@ -501,15 +501,6 @@ struct GemmPlan {
 
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
-// Tokens are split into ceil(T / 256) equal tiles (UMMA N <= 256, a multiple
-// of 16); rows of h into 128-row tiles.  If the tiles leave SMs idle, the
-// compressed width is split first (a cluster of up to 8 CTAs per tile: every
-// weight byte is still loaded once); only if that still fills less than half
-// the SMs are the token tiles halved (down to 32 tokens: each halving makes
-// one more CTA load the same weight tile).  Token tiles of <= 64 take two
-// 64-column atoms per stage, so one barrier round trip of the producer and
-// MMA threads feeds 8 MMAs instead of 4.  The ring takes as many stages
-// (<= 8) as shared memory holds.
 // Clusters of `size` CTAs (one tile's k-splits) that can be resident at
 // once with `smem` bytes of dynamic shared memory each; clusters are placed
 // inside one GPC, so some sizes leave SMs unusable.  Cached per device.
@@ -545,46 +536,108 @@ int gemm_max_clusters(int size, size_t smem, int* out) {
   return NMS_OK;
 }
 
-int gemm_plan(int64_t T, int64_t w_pad, int64_t h, int num_sms, size_t smem_max, GemmPlan* g) {
-  g->n_tiles = (int32_t)((T + nms::kGemmMaxBN - 1) / nms::kGemmMaxBN);
-  g->bn = (int32_t)std::max<int64_t>(16, round_up((T + g->n_tiles - 1) / g->n_tiles, 16));
-  g->m_tiles = (int32_t)((h + nms::kGemmBM - 1) / nms::kGemmBM);
-  int64_t tiles = 0;
-  auto fill = [&]() {
-    tiles = (int64_t)g->m_tiles * g->n_tiles;
-    g->splits = tiles < num_sms ? (int32_t)std::min<int64_t>(8, num_sms / tiles) : 1;
-  };
-  fill();
-  while (g->bn >= 64 && tiles * g->splits * 2 <= num_sms) {
-    g->bn = (int32_t)round_up(g->bn / 2, 16);
-    g->n_tiles = (int32_t)((T + g->bn - 1) / g->bn);
-    fill();
-  }
-  g->atoms = g->bn <= 64 ? 2 : 1;
-  g->kblocks = (int32_t)((w_pad / nms::kGemmBK + g->atoms - 1) / g->atoms);
-  if (g->splits > g->kblocks) g->splits = g->kblocks;
-  if (g->splits < 1) g->splits = 1;
-  const size_t stage = ((size_t)nms::kGemmBM * 128 + (size_t)g->bn * 128) * g->atoms;
+// One candidate shape of the prefill GEMM grid: token tiles of `bn`, `splits`
+// k-splits per tile (a cluster), and its estimated time.  Measured on B200
+// (per-CTA traces): the single producer and MMA-issuing threads pace a stage
+// at ~0.45 us whatever its width, and the split-K epilogue (two cluster
+// barriers, the distributed-shared-memory push and the reduction) costs
+// ~1 us + 0.05 us per token column of the tile.
+struct GemmCand {
+  int32_t bn = 0, n_tiles = 0, atoms = 1, kblocks = 0, splits = 1, stages = 0;
+  size_t smem = 0;
+  int64_t ctas = 0, waves = 0, cost = 0;  // cost in units of 0.01 us
+};
+
+int gemm_candidate(int64_t T, int64_t w_pad, int32_t m_tiles, int32_t bn, int32_t splits_max, int num_sms,
+                   size_t smem_max, GemmCand* c, bool* ok) {
+  *ok = false;
+  c->bn = bn;
+  c->n_tiles = (int32_t)((T + bn - 1) / bn);
+  c->atoms = bn <= 64 ? 2 : 1;
+  c->kblocks = (int32_t)((w_pad / nms::kGemmBK + c->atoms - 1) / c->atoms);
+  const size_t stage = ((size_t)nms::kGemmBM * 128 + (size_t)bn * 128) * c->atoms;
   const size_t avail = smem_max > 1024 ? smem_max - 1024 : 0;
-  g->stages = (int32_t)std::min<size_t>(nms::kGemmMaxStages, avail / stage);
-  if (g->stages < 2) return fail(NMS_ERR_NOT_IMPLEMENTED, "gemm: %zu B of shared memory holds fewer than 2 stages", smem_max);
-  g->smem = 1024 + (size_t)g->stages * stage;
+  c->stages = (int32_t)std::min<size_t>(nms::kGemmMaxStages, avail / stage);
+  if (c->stages < 2) return NMS_OK;
+  c->smem = 1024 + (size_t)c->stages * stage;
+  const int64_t tiles = (int64_t)m_tiles * c->n_tiles;
+  c->splits = (int32_t)std::max<int64_t>(1, std::min<int64_t>(splits_max, c->kblocks));
   // Keep every tile's cluster resident in one wave: shrink the split count
   // until the GPCs hold `tiles` clusters of that size.
-  while (g->splits > 1) {
+  while (c->splits > 1) {
     int fit = 0;
-    int rc = gemm_max_clusters(g->splits, g->smem, &fit);
+    int rc = gemm_max_clusters(c->splits, c->smem, &fit);
     if (rc) return rc;
     if (fit >= tiles) break;
-    --g->splits;
+    --c->splits;
   }
   // Epilogue staging reuses the ring: fp16 output rows, after the split-K
   // receive buffer (splits x 128 rows x (owned columns + 4) fp32) when split.
-  const int64_t ncl = (g->bn / 16 + g->splits - 1) / g->splits * 16;
-  const size_t staging = g->splits > 1 ? (size_t)g->splits * nms::kGemmBM * (ncl + 4) * 4 + (size_t)ncl * nms::kGemmOutPitch * 2
-                                       : (size_t)g->bn * nms::kGemmOutPitch * 2;
-  if (staging > (size_t)g->stages * stage)
-    return fail(NMS_ERR_NOT_IMPLEMENTED, "gemm: epilogue staging of %zu B exceeds the ring", staging);
+  const int64_t ncl = (bn / 16 + c->splits - 1) / c->splits * 16;
+  const size_t staging = c->splits > 1
+                             ? (size_t)c->splits * nms::kGemmBM * (ncl + 4) * 4 + (size_t)ncl * nms::kGemmOutPitch * 2
+                             : (size_t)bn * nms::kGemmOutPitch * 2;
+  if (staging > (size_t)c->stages * stage) return NMS_OK;
+  c->ctas = tiles * c->splits;
+  c->waves = (c->ctas + num_sms - 1) / num_sms;  // one CTA per SM (shared memory)
+  const int64_t per_cta = (c->kblocks + c->splits - 1) / c->splits * 45 + (c->splits > 1 ? 100 + 5 * bn : 0);
+  c->cost = c->waves * per_cta;
+  *ok = true;
+  return NMS_OK;
+}
+
+// Tokens are split into ceil(T / 256) equal tiles (UMMA N <= 256, a multiple
+// of 16); rows of h into 128-row tiles.  The default plan splits the
+// compressed width when the tiles leave SMs idle (a cluster of up to 8 CTAs
+// per tile: every weight byte is still loaded once), and halves the token
+// tiles (down to 32) only while that still fills less than half the SMs.
+// Other candidates -- each halving of the token tile, unsplit or split -- are
+// costed with the model above, and one replaces the default only if it is
+// estimated at least 10% faster (ties: fewer waves, then more CTAs).  Token
+// tiles of <= 64 take two 64-column atoms per stage, so one barrier round
+// trip of the producer and MMA threads feeds 8 MMAs instead of 4.
+int gemm_plan(int64_t T, int64_t w_pad, int64_t h, int num_sms, size_t smem_max, GemmPlan* g) {
+  g->m_tiles = (int32_t)((h + nms::kGemmBM - 1) / nms::kGemmBM);
+  const int32_t n0 = (int32_t)((T + nms::kGemmMaxBN - 1) / nms::kGemmMaxBN);
+  const int32_t bn0 = (int32_t)std::max<int64_t>(16, round_up((T + n0 - 1) / n0, 16));
+  auto smax = [&](int32_t bn) -> int32_t {
+    const int64_t tiles = (int64_t)g->m_tiles * ((T + bn - 1) / bn);
+    return tiles < num_sms ? (int32_t)std::min<int64_t>(8, num_sms / tiles) : 1;
+  };
+  // The default plan.
+  int32_t bn_def = bn0;
+  while (bn_def >= 64 && (int64_t)g->m_tiles * ((T + bn_def - 1) / bn_def) * smax(bn_def) * 2 <= num_sms)
+    bn_def = (int32_t)round_up(bn_def / 2, 16);
+  GemmCand best;
+  bool ok = false;
+  int rc = gemm_candidate(T, w_pad, g->m_tiles, bn_def, smax(bn_def), num_sms, smem_max, &best, &ok);
+  if (rc) return rc;
+  if (!ok) return fail(NMS_ERR_NOT_IMPLEMENTED, "gemm: no grid fits %zu B of shared memory", smem_max);
+  const int64_t def_cost = best.cost;
+  GemmCand alt;
+  bool have_alt = false;
+  for (int32_t bn = bn0;; bn = (int32_t)round_up(bn / 2, 16)) {
+    for (int32_t sm : {1, smax(bn)}) {
+      GemmCand c;
+      rc = gemm_candidate(T, w_pad, g->m_tiles, bn, sm, num_sms, smem_max, &c, &ok);
+      if (rc) return rc;
+      if (!ok || (c.bn == best.bn && c.splits == best.splits)) continue;
+      if (!have_alt || c.cost < alt.cost ||
+          (c.cost == alt.cost && (c.waves < alt.waves || (c.waves == alt.waves && c.ctas > alt.ctas)))) {
+        alt = c;
+        have_alt = true;
+      }
+    }
+    if (bn < 64) break;
+  }
+  if (have_alt && alt.cost * 10 <= def_cost * 9) best = alt;
+  g->bn = best.bn;
+  g->n_tiles = best.n_tiles;
+  g->atoms = best.atoms;
+  g->kblocks = best.kblocks;
+  g->splits = best.splits;
+  g->stages = best.stages;
+  g->smem = best.smem;
   g->total = round_up(T * w_pad * 2, 256);
   return NMS_OK;
 }
