@@ -184,3 +184,13 @@ def test_gemm_op_rejects_cpu_tensors():
                                            torch.empty(384, 128, dtype=torch.float16),
                                            torch.empty(8, 16, dtype=torch.uint8), 128, 384, 16, 32)
         assert tuple(y.shape) == (3, 5, 384) and y.dtype == torch.bfloat16
+
+
+@pytest.mark.parametrize("T,w_pad,h,msg", [(0, 2048, 4096, "positive"), (16, 2000, 4096, "multiple of 64"),
+                                           (16, 2048, 0, "positive")])
+def test_gemm_workspace_argument_validation(T, w_pad, h, msg):
+    n = ctypes.c_int64(-1)
+    rc = _lib.lib().nms_gemm_workspace_bytes(T, w_pad, h, ctypes.byref(n))
+    assert rc == _lib.NMS_ERR_VALUE and n.value == -1
+    assert msg in _lib.lib().nms_last_error().decode()
+    assert _lib.lib().nms_gemm_workspace_bytes(16, 2048, 4096, None) == _lib.NMS_ERR_VALUE
