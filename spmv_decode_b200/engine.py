@@ -43,6 +43,10 @@ ARGMAX_CAPACITY = 2048
 def _linear_segment(lin) -> dict:
     """Segment description (packed weights, mask, rows, shape) of a linear."""
     if isinstance(lin, NmSparseLinear):
+        if lin.layout != "shared":
+            raise NotImplementedError(
+                "the decode engine fuses shared-mask layers; per-row (layout='rowwise') layers decode "
+                "through nmsparse::gemv in the model's own forward")
         return dict(packed=lin.mat_data, idx=lin.mat_index, rows=lin.h, K=lin.in_features, w=lin.w,
                     w_pad=lin.w_pad, n=lin.block_width, m=lin.vec_width, dense=False)
     if isinstance(lin, nn.Linear) or hasattr(lin, "weight"):

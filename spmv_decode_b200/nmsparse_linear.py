@@ -36,8 +36,13 @@ from .nmsparse_op import pack, packed_row_stride, unpack
 
 DECODE_ONLY = os.environ.get("NM_DECODE_ONLY", "0") == "1"
 WEIGHT_CPU = os.environ.get("NM_WEIGHT_CPU", "0") == "1" or DECODE_ONLY
+# NM_KERNEL=fp16 / fp16_split select the reference's per-row layout
+# (src/spmv/nmsparse_linear.py:9-11, 27-29); anything else accepted here
+# (unset, triton_ptx) is the shared-mask layout.
+DEFAULT_LAYOUT = "rowwise" if os.environ.get("NM_KERNEL", "") in ("fp16", "fp16_split") else "shared"
 
-LAYOUT_PACKED = 1
+LAYOUT_PACKED = 1   # shared mask, values re-laid-out as packed [h, w_pad]
+LAYOUT_ROWWISE = 2  # per-row offsets, values in the reference layout [w, h]
 
 _SPARSE_PREFILL = False
 
@@ -58,21 +63,30 @@ def sparse_prefill(enabled: bool = True):
         _SPARSE_PREFILL = old
 
 
-def make_sparse(K: int, N: int, M: int, seed: int, device="cpu"):
-    """Synthetic shared-mask N:M weights, bit-exact with the reference packer.
+def make_sparse(K: int, N: int, M: int, seed: int, device="cpu", *, layout: str = "shared"):
+    """Synthetic N:M weights, bit-exact with the reference packer.
 
-    Returns ``(mat_data [w, N] fp16, mat_index [K/M, M/2] uint8, w, nnz)`` on
-    ``device``; 50% sparsity (nnz = M/2) as in the reference
-    (src/spmv/nmsparse_linear.py:14-33, shared-mask branch :22-26).
+    ``layout="shared"`` (NM_KERNEL=triton_ptx): returns ``(mat_data [w, N]
+    fp16, mat_index [K/M, M/2] uint8, w, nnz)`` -- one sorted random mask per
+    group of M inputs shared by every output row (src/spmv/nmsparse_linear.py:14-33,
+    branch :22-26).  ``layout="rowwise"`` (NM_KERNEL=fp16 / fp16_split): the
+    same values and an offset in [0, M) drawn per value, ``mat_index [w, N]``
+    uint8 (branch :27-29); offsets may repeat within a group, and the product
+    then adds both values at that input.  50% sparsity (nnz = M/2) either way.
     """
+    if layout not in ("shared", "rowwise"):
+        raise ValueError(f"unknown layout={layout!r}")
     nnz = M // 2
     nb = K // M
     w = nb * nnz
     g = torch.Generator().manual_seed(seed)
     mat_data = (torch.randn(w, N, generator=g, dtype=torch.float32) / (K ** 0.5)).to(torch.float16)
-    mat_index = torch.empty(nb, nnz, dtype=torch.uint8)
-    for bank in range(nb):
-        mat_index[bank] = torch.randperm(M, generator=g)[:nnz].sort().values.to(torch.uint8)
+    if layout == "rowwise":
+        mat_index = torch.randint(0, M, (w, N), generator=g, dtype=torch.uint8)
+    else:
+        mat_index = torch.empty(nb, nnz, dtype=torch.uint8)
+        for bank in range(nb):
+            mat_index[bank] = torch.randperm(M, generator=g)[:nnz].sort().values.to(torch.uint8)
     if str(device) != "cpu":
         mat_data = mat_data.to(device)
         mat_index = mat_index.to(device)
@@ -117,6 +131,19 @@ def masked_dense(mat_data: torch.Tensor, mat_index: torch.Tensor, K: int, M: int
     return dense
 
 
+def rowwise_masked_dense(mat_data: torch.Tensor, mat_index: torch.Tensor, K: int, M: int) -> torch.Tensor:
+    """Dense [h, K] weight of the per-row layout (values [w, h], offsets
+    [w, h]): value (j, r) added at column (j / N) * M + offset, N = w / (K / M).
+    Repeated offsets accumulate, as the per-row product does."""
+    w, h = mat_data.shape
+    n = w // (K // M)
+    base = (torch.arange(w, device=mat_index.device) // n * M).unsqueeze(1)
+    cols = (base + mat_index.long()).t()  # [h, w]
+    dense = torch.zeros((h, K), dtype=torch.float32, device=mat_data.device)
+    dense.scatter_add_(1, cols.to(mat_data.device), mat_data.t().float())
+    return dense.to(mat_data.dtype)
+
+
 def make_rowwise_topk(weight: torch.Tensor, n: int, m: int):
     """Per-row top-|w| N:M packing of a dense [h, K] weight:
     for every row and group of m consecutive input columns keep the n largest
@@ -138,10 +165,21 @@ def make_rowwise_topk(weight: torch.Tensor, n: int, m: int):
 
 
 class NmSparseLinear(nn.Module):
-    """Shared-mask 50% N:M sparse linear (reference: src/spmv/nmsparse_linear.py:36-68)."""
+    """50% N:M sparse linear (reference: src/spmv/nmsparse_linear.py:36-68).
 
-    def __init__(self, N, K, M, seed, device, dense_weight=None, *, init: str = "reference"):
+    ``layout="shared"`` (default unless NM_KERNEL is fp16 / fp16_split): one
+    mask per input group shared by all rows, values stored packed [h, w_pad]
+    for the sm_100a GEMV and GEMM.  ``layout="rowwise"``: the reference's
+    per-row layout, values [w, h] and offsets [w, h], decoded by the per-row
+    kernel behind ``nmsparse::gemv``."""
+
+    def __init__(self, N, K, M, seed, device, dense_weight=None, *, init: str = "reference",
+                 layout: str | None = None):
         super().__init__()
+        layout = DEFAULT_LAYOUT if layout is None else layout
+        if layout not in ("shared", "rowwise"):
+            raise ValueError(f"unknown layout={layout!r}")
+        self.layout = layout
         assert K % M == 0 and N % 128 == 0, (K, N, M)
         self._weight_cpu = None
         self.weight = None
@@ -153,7 +191,21 @@ class NmSparseLinear(nn.Module):
                     torch.cuda.empty_cache()
             else:
                 self.weight = dense_weight
-        if init == "reference":
+        if layout == "rowwise":
+            nnz = M // 2
+            w = (K // M) * nnz
+            if init == "reference":
+                packed, mi, w, nnz = make_sparse(K, N, M, seed, device, layout="rowwise")
+            elif init == "device":
+                gen = torch.Generator(device=device).manual_seed(seed)
+                packed = (torch.randn((w, N), generator=gen, device=device) / (K ** 0.5)).to(torch.float16)
+                mi = torch.randint(0, M, (w, N), generator=gen, device=device, dtype=torch.uint8)
+            elif init == "empty":
+                packed = torch.zeros((w, N), dtype=torch.float16, device=device)
+                mi = torch.zeros((w, N), dtype=torch.uint8, device=device)
+            else:
+                raise ValueError(f"unknown init={init!r}")
+        elif init == "reference":
             md, mi, w, nnz = make_sparse(K, N, M, seed, device)
             packed = pack(md)
             del md
@@ -168,20 +220,24 @@ class NmSparseLinear(nn.Module):
             raise ValueError(f"unknown init={init!r}")
         self.register_buffer("mat_data", packed)
         self.register_buffer("mat_index", mi)
-        self.register_buffer("mat_layout", torch.tensor([LAYOUT_PACKED], dtype=torch.uint8, device=packed.device))
+        code = LAYOUT_ROWWISE if layout == "rowwise" else LAYOUT_PACKED
+        self.register_buffer("mat_layout", torch.tensor([code], dtype=torch.uint8, device=packed.device))
         self.h, self.w, self.block_width, self.vec_width = N, w, nnz, M
         self.in_features, self.out_features = K, N
 
     @property
     def w_pad(self) -> int:
-        return int(self.mat_data.shape[-1])
+        """Row stride of the packed values (shared layout); w for per-row."""
+        return self.w if self.layout == "rowwise" else int(self.mat_data.shape[-1])
 
     def reference_mat_data(self) -> torch.Tensor:
         """The kept values in the reference layout [w, h] (bit-exact)."""
-        return unpack(self.mat_data, self.w)
+        return self.mat_data if self.layout == "rowwise" else unpack(self.mat_data, self.w)
 
     def dense_masked_weight(self) -> torch.Tensor:
         """[h, K] dense weight holding the kept values (zeros elsewhere)."""
+        if self.layout == "rowwise":
+            return rowwise_masked_dense(self.mat_data, self.mat_index, self.in_features, self.vec_width)
         return masked_dense(self.reference_mat_data(), self.mat_index, self.in_features, self.vec_width)
 
     def _prefill_weight(self, device):
@@ -193,11 +249,17 @@ class NmSparseLinear(nn.Module):
 
     def forward(self, x):
         if x.shape[-2] == 1:
+            if self.layout == "rowwise":
+                return torch.ops.nmsparse.gemv(
+                    x, self.mat_data, self.mat_index,
+                    self.w, self.h, self.block_width, self.vec_width,
+                )
             return torch.ops.nmsparse.gemv_packed(
                 x, self.mat_data, self.mat_index,
                 self.w, self.h, self.block_width, self.vec_width,
             )
-        if x.is_cuda and (_SPARSE_PREFILL or (self.weight is None and self._weight_cpu is None)):
+        if self.layout == "shared" and x.is_cuda and (
+                _SPARSE_PREFILL or (self.weight is None and self._weight_cpu is None)):
             # No dense weight kept (the reference raises here, :57-61), or
             # inside sparse_prefill(): the sparse layer on the tensor cores.
             return torch.ops.nmsparse.gemm_packed(
@@ -210,7 +272,10 @@ class NmSparseLinear(nn.Module):
                               unexpected_keys, error_msgs):
         # A reference state dict has mat_data in [w, h] and no layout marker.
         key_d, key_l = prefix + "mat_data", prefix + "mat_layout"
-        if key_d in state_dict and key_l not in state_dict:
+        if self.layout == "rowwise":
+            if key_d in state_dict and key_l not in state_dict:
+                state_dict[key_l] = torch.tensor([LAYOUT_ROWWISE], dtype=torch.uint8)
+        elif key_d in state_dict and key_l not in state_dict:
             md = state_dict[key_d]
             if tuple(md.shape) == (self.w, self.h):
                 state_dict[key_d] = pack(md.to(torch.float16), self.w_pad)
@@ -220,7 +285,7 @@ class NmSparseLinear(nn.Module):
 
     def extra_repr(self) -> str:
         return (f"in={self.in_features}, out={self.h}, {self.block_width}:{self.vec_width}, "
-                f"w={self.w}, w_pad={self.w_pad}")
+                f"w={self.w}, w_pad={self.w_pad}, layout={self.layout}")
 
 
 # Block layouts swap_to_nmsparse knows (reference :83-91): gpt-fast fused
@@ -250,7 +315,7 @@ def _resolve_layout(blk, layouts, kind):
     )
 
 
-def _swap_linears(submodule, linear_names, M, device, seed, cnt, init, keep_dense):
+def _swap_linears(submodule, linear_names, M, device, seed, cnt, init, keep_dense, layout):
     for name in linear_names:
         old = getattr(submodule, name)
         if isinstance(old, NmSparseLinear):
@@ -262,13 +327,14 @@ def _swap_linears(submodule, linear_names, M, device, seed, cnt, init, keep_dens
         del old
         if torch.cuda.is_available():
             torch.cuda.empty_cache()
-        setattr(submodule, name, NmSparseLinear(N, K, M, seed + cnt, device, dense_weight=dense_weight, init=init))
+        setattr(submodule, name, NmSparseLinear(N, K, M, seed + cnt, device, dense_weight=dense_weight, init=init,
+                                                layout=layout))
         cnt += 1
     return cnt
 
 
 def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str = "reference",
-                     keep_dense: bool | None = None):
+                     keep_dense: bool | None = None, layout: str | None = None):
     """Replace every decoder block's attention and MLP linears with
     NmSparseLinear (reference: src/spmv/nmsparse_linear.py:124-144).
 
@@ -278,7 +344,8 @@ def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str 
     ``init="device"`` draws the weights on the GPU instead (same
     distribution, different numbers, much faster for multi-GB models).
     ``keep_dense`` overrides NM_DECODE_ONLY for keeping the dense weight (used
-    by prefill with more than one token, :55-68).
+    by prefill with more than one token, :55-68).  ``layout`` ("shared" or
+    "rowwise") overrides the NM_KERNEL default of NmSparseLinear.
     """
     cnt = 0
     for i, blk in enumerate(model.layers):
@@ -287,7 +354,7 @@ def swap_to_nmsparse(model, M, device, seed=0, block_devices=None, *, init: str 
             d = block_devices[i]
             blk_device = d if isinstance(d, str) else f"cuda:{d}"
         attn, attn_names = _resolve_layout(blk, _ATTENTION_LAYOUTS, "attention")
-        cnt = _swap_linears(attn, attn_names, M, blk_device, seed, cnt, init, keep_dense)
+        cnt = _swap_linears(attn, attn_names, M, blk_device, seed, cnt, init, keep_dense, layout)
         mlp, mlp_names = _resolve_layout(blk, _MLP_LAYOUTS, "feed-forward")
-        cnt = _swap_linears(mlp, mlp_names, M, blk_device, seed, cnt, init, keep_dense)
+        cnt = _swap_linears(mlp, mlp_names, M, blk_device, seed, cnt, init, keep_dense, layout)
     return cnt

@@ -4,9 +4,12 @@ Drop-in for the reference operator boundary (src/spmv/nmsparse_op.py:77-123):
 same op name, same signature, same fake kernel, same argument meaning and
 the same exception types for the same conditions.  The reference selected a
 backend from ``NM_KERNEL``; here there is exactly one backend and no
-fallback, so ``NM_KERNEL`` is accepted only as unset or ``triton_ptx`` (the
-reference's shared-mask mode, whose layout this implements) and anything else
-raises ``ValueError`` like the reference's allow-list (src/spmv/nmsparse_op.py:20-22).
+fallback.  ``NM_KERNEL`` unset or ``triton_ptx`` selects the shared-mask
+layout, ``fp16`` or ``fp16_split`` the per-row layout (values [w, h], offsets
+[w, h], served by the per-row kernel: the reference names CUDA kernels for it
+that it does not ship); anything else -- ``guarded``, a CUDA-guard build for
+tensor parallelism, or a typo -- raises ``ValueError`` like the reference's
+allow-list (src/spmv/nmsparse_op.py:20-22).
 
 Also registers ``nmsparse::gemv_packed`` for the re-laid-out weights that
 ``NmSparseLinear`` stores (packed [h, w_pad] rows, see include/nmsparse_b200.h),
@@ -23,10 +26,10 @@ import torch
 from . import _lib
 
 _kernel = os.environ.get("NM_KERNEL", "")
-if _kernel not in ("", "triton_ptx"):
+if _kernel not in ("", "triton_ptx", "fp16", "fp16_split"):
     raise ValueError(
-        f"Unknown NM_KERNEL={_kernel!r}; this build has one CUDA backend "
-        "(the shared-mask layout of NM_KERNEL=triton_ptx) and refuses silent fallback"
+        f"Unknown NM_KERNEL={_kernel!r}; this build has one CUDA backend (shared-mask layout for "
+        "NM_KERNEL unset / triton_ptx, per-row layout for fp16 / fp16_split) and refuses silent fallback"
     )
 _mode = "b200_cuda"
 

@@ -9,6 +9,9 @@ What it records, all produced by the reference's own code:
   packer.npz    -- _make_sparse (src/spmv/nmsparse_linear.py:14-33, shared-mask
                    branch, NM_KERNEL=triton_ptx): full arrays for small shapes,
                    SHA-256 of the bytes plus leading values for Llama shapes.
+  packer_rowwise.npz -- _make_sparse's per-row branch (the layout of
+                   NM_KERNEL=fp16 / fp16_split: mat_data [w, N] fp16 and
+                   per-value offsets mat_index [w, N] uint8), same recording.
   gemv.npz      -- outputs of the reference Triton kernels
                    nmsparse_generic_kernel and nmsparse_a100_sm80_kernel
                    (triton_spmv.py:40-214), executed by the Triton interpreter
@@ -118,6 +121,32 @@ def make_packer():
         out[f"big{i}_head_index"] = mi[:2].numpy()
     np.savez_compressed(HERE / "packer.npz", **out)
     print("packer.npz:", len(small), "small,", len(big), "big")
+
+
+def make_packer_rowwise():
+    """_make_sparse reads its mode from module globals at call time; switch
+    them to what NM_KERNEL=fp16_split sets (src/spmv/nmsparse_linear.py:9-11)."""
+    saved = (ref_linear._SHARED_MASK, ref_linear._FP16_SPARSE)
+    ref_linear._SHARED_MASK, ref_linear._FP16_SPARSE = False, True
+    try:
+        out = {}
+        small = [(256, 128, 4, 0), (512, 256, 16, 2), (1024, 128, 64, 4), (2048, 128, 256, 6)]
+        for i, (K, N, M, seed) in enumerate(small):
+            md, mi, w, nnz = ref_linear._make_sparse(K, N, M, seed, "cpu")
+            assert md.dtype == torch.float16 and tuple(mi.shape) == (w, N)
+            out[f"small{i}_cfg"] = np.array([K, N, M, seed, w, nnz], dtype=np.int64)
+            out[f"small{i}_mat_data"] = md.view(torch.int16).numpy()
+            out[f"small{i}_mat_index"] = mi.numpy()
+        big = [(4096, 4096, 64, 0), (14336, 4096, 64, 4)]
+        for i, (K, N, M, seed) in enumerate(big):
+            md, mi, w, nnz = ref_linear._make_sparse(K, N, M, seed, "cpu")
+            out[f"big{i}_cfg"] = np.array([K, N, M, seed, w, nnz], dtype=np.int64)
+            out[f"big{i}_sha_data"] = np.frombuffer(bytes.fromhex(sha(md.view(torch.int16))), dtype=np.uint8)
+            out[f"big{i}_sha_index"] = np.frombuffer(bytes.fromhex(sha(mi)), dtype=np.uint8)
+        np.savez_compressed(HERE / "packer_rowwise.npz", **out)
+        print("packer_rowwise.npz:", len(small), "small,", len(big), "big")
+    finally:
+        ref_linear._SHARED_MASK, ref_linear._FP16_SPARSE = saved
 
 
 def make_gemv():
@@ -257,9 +286,11 @@ def make_decode_qwen3(steps=24, prompt_len=8):
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["packer", "gemv", "llama", "qwen3"]
+    which = sys.argv[1:] or ["packer", "rowwise", "gemv", "llama", "qwen3"]
     if "packer" in which:
         make_packer()
+    if "rowwise" in which:
+        make_packer_rowwise()
     if "gemv" in which:
         make_gemv()
     if "llama" in which:

@@ -52,3 +52,35 @@ def test_rowwise_shapes(cuda_device, shape):
     x = torch.randn(1, K, generator=g, device=cuda_device).to(torch.float16)
     y, ref = _run(W, x, 32, 64, cuda_device)
     assert _max_rel(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("M", [16, 64])
+def test_rowwise_module_with_the_reference_packer(cuda_device, M):
+    """NmSparseLinear(layout="rowwise") holds the reference packer's per-row
+    values and offsets (NM_KERNEL=fp16_split layout, repeated offsets
+    included) and decodes through nmsparse::gemv's per-row kernel."""
+    from spmv_decode_b200.nmsparse_linear import NmSparseLinear
+
+    K, N = 4096, 4096
+    lin = NmSparseLinear(N, K, M, 0, cuda_device, layout="rowwise")
+    x = torch.randn(1, 1, K, generator=torch.Generator().manual_seed(M)).to(torch.float16)
+    y = lin(x.to(cuda_device))
+    assert y.shape == (1, 1, N) and y.dtype == torch.float16
+    ref = rowwise_gemv_fp32(x.numpy().reshape(-1), lin.mat_data.cpu().numpy(), lin.mat_index.cpu().numpy(),
+                            M // 2, M)
+    assert _max_rel(y.cpu().numpy().reshape(-1), ref) <= TOL
+
+
+def test_engine_refuses_rowwise_layers(cuda_device):
+    from spmv_decode_b200.engine import DecodeEngine
+    from spmv_decode_b200.model import ModelArgs, Transformer
+    from spmv_decode_b200.nmsparse_linear import swap_to_nmsparse
+
+    args = ModelArgs(block_size=64, vocab_size=256, n_layer=1, n_head=2, n_local_heads=1, dim=256,
+                     intermediate_size=512)
+    with torch.device(cuda_device):
+        model = Transformer(args)
+    model = model.half()
+    swap_to_nmsparse(model, 32, cuda_device, layout="rowwise")
+    with pytest.raises(NotImplementedError, match="per-row"):
+        DecodeEngine(model, 32)
