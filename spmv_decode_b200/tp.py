@@ -49,7 +49,7 @@ class DenseShard(nn.Module):
 
 
 def _sparse_like(packed: torch.Tensor, mat_index: torch.Tensor, K: int, N: int, M: int) -> NmSparseLinear:
-    lin = NmSparseLinear(N, K, M, 0, packed.device, init="empty")
+    lin = NmSparseLinear(N, K, M, 0, packed.device, init="empty", layout="shared")
     lin.mat_data = packed.contiguous()
     lin.mat_index = mat_index.contiguous()
     lin.w = mat_index.shape[0] * mat_index.shape[1]
@@ -57,9 +57,16 @@ def _sparse_like(packed: torch.Tensor, mat_index: torch.Tensor, K: int, N: int, 
     return lin
 
 
+def _shared_only(lin: NmSparseLinear) -> None:
+    if lin.layout != "shared":
+        raise NotImplementedError("tensor-parallel shards are built from shared-mask layers; "
+                                  "per-row (layout='rowwise') layers are not sharded")
+
+
 def shard_rows(lin: nn.Module, ranges) -> nn.Module:
     """Rows ``ranges`` ([(r0, r1), ...], concatenated in order) of a linear."""
     if isinstance(lin, NmSparseLinear):
+        _shared_only(lin)
         packed = torch.cat([lin.mat_data[r0:r1] for r0, r1 in ranges])
         return _sparse_like(packed, lin.mat_index, lin.in_features, packed.shape[0], lin.vec_width)
     return DenseShard(torch.cat([lin.weight.detach()[r0:r1] for r0, r1 in ranges]))
@@ -70,6 +77,7 @@ def shard_cols(lin: nn.Module, k0: int, k1: int) -> nn.Module:
     whole mask groups, and the shard keeps their compressed columns and
     mask rows (re-padded to the packed row stride)."""
     if isinstance(lin, NmSparseLinear):
+        _shared_only(lin)
         M, n = lin.vec_width, lin.block_width
         if k0 % M or k1 % M:
             raise ValueError(f"column shard [{k0}, {k1}) is not made of whole {M}-column mask groups")

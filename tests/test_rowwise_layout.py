@@ -71,3 +71,16 @@ def test_rowwise_state_dict_and_multi_token_rule():
     torch.testing.assert_close(c(x), F.linear(x, dense))
     with pytest.raises(ValueError):
         NmSparseLinear(N, K, M, 1, "cpu", layout="diagonal")
+
+
+def test_tensor_parallel_sharding_refuses_rowwise_layers():
+    from spmv_decode_b200.tp import shard_cols, shard_rows
+
+    lin = NmSparseLinear(256, 512, 32, 0, "cpu", layout="rowwise")
+    with pytest.raises(NotImplementedError, match="per-row"):
+        shard_rows(lin, [(0, 128)])
+    with pytest.raises(NotImplementedError, match="per-row"):
+        shard_cols(lin, 0, 256)
+    shared = NmSparseLinear(256, 512, 32, 0, "cpu", layout="shared")
+    part = shard_rows(shared, [(0, 128)])
+    assert part.layout == "shared" and part.h == 128
