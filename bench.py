@@ -237,6 +237,20 @@ def emit(line: dict) -> None:
         os.write(_JSON_FD, data)
 
 
+def result_line(ctx: int, nm: str, mode: str, warmup: int, steps: int, ms: float) -> str:
+    """The reference benchmark's summary line (benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:186-189),
+    the one its runner scripts parse (scripts/run_bench_qwen_32b_fp16.sh:215-219).  The timed
+    region is one sample (the mean over ``steps`` replays), so median = mean and stdev = 0."""
+    if nm == "dense":
+        tag = "dense_float16"
+    else:
+        n, m = nm.split(":")
+        tag = f"M={m}({n}:{m})"
+    return (f"RESULT CTX={ctx} {tag} dtype=float16 actual_mode=b200_{mode} "
+            f"measurement=fixed_context_cuda_graph warmup={warmup} repeat=1 "
+            f"decode_ms_per_token={ms:.6f} mean={ms:.6f} stdev=0.000000")
+
+
 def main():
     global _JSON_FD
     args = parse_args()
@@ -455,6 +469,8 @@ def main():
             "device_error": dev_err,
         }
         emit(line)
+        # stdout carries only the JSON line; the reference's RESULT line goes to stderr.
+        print(result_line(args.ctx, args.nm, engine_mode, args.warmup, args.steps, ms), file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier()
         tp.close()
