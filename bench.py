@@ -58,15 +58,36 @@ PUBLISHED = {("llama-3.1-8b", "32:64"): (6.8521, "A100-SXM4-80GB", "README.md:93
              ("qwen3-32b", "16:32"): (33.7054, "A100-SXM4-80GB", "README.md:118")}
 
 
+def env_defaults() -> dict:
+    """Defaults from the reference benchmark's environment (benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:97-105):
+    NM_M (0 = dense, else M with N = M/2), CTX, BENCH_WARMUP, and BENCH_REPEAT x BENCH_INNER timed
+    replays.  Only variables that are set apply; explicit flags override them."""
+    env = os.environ
+    d = {"ctx": int(env.get("CTX", 512))}
+    if "NM_M" in env:
+        m = int(env["NM_M"])
+        if m not in (0, 4, 8, 16, 32, 64, 128, 256):
+            raise ValueError("Unsupported NM_M")
+        d["nm"] = "dense" if m == 0 else f"{m // 2}:{m}"
+    if "BENCH_WARMUP" in env:
+        d["warmup"] = int(env["BENCH_WARMUP"])
+    if "BENCH_REPEAT" in env or "BENCH_INNER" in env:
+        d["steps"] = int(env.get("BENCH_REPEAT", "30")) * int(env.get("BENCH_INNER", "10"))
+    if min(d["ctx"], d.get("warmup", 1), d.get("steps", 1)) < 1:
+        raise ValueError("CTX, warmup, repeat, inner must be positive")
+    return d
+
+
 def parse_args():
+    env = env_defaults()
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=1000)
-    p.add_argument("--warmup", type=int, default=50)
+    p.add_argument("--steps", type=int, default=env.get("steps", 1000))
+    p.add_argument("--warmup", type=int, default=env.get("warmup", 50))
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--model", default="llama-3.1-8b")
-    p.add_argument("--nm", default="32:64", help="N:M pattern, or 'dense'")
-    p.add_argument("--ctx", type=int, default=int(os.environ.get("CTX", 512)))
+    p.add_argument("--nm", default=env.get("nm", "32:64"), help="N:M pattern, or 'dense'")
+    p.add_argument("--ctx", type=int, default=env["ctx"])
     p.add_argument("--e2e-steps", type=int, default=256)
     p.add_argument("--prefetch", type=int, default=0, help="per-warp L2 look-ahead bytes inside a GEMV")
     p.add_argument("--next-prefetch", type=int, default=0,
