@@ -272,9 +272,23 @@ def result_line(ctx: int, nm: str, mode: str, warmup: int, steps: int, ms: float
             f"decode_ms_per_token={ms:.6f} mean={ms:.6f} stdev=0.000000")
 
 
+def check_import_origin() -> None:
+    """Time only this tree: the package and its native library must come from
+    the directory bench.py sits in, not a stray installed copy (the reference's
+    "Foreign import" guard, benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:91-94)."""
+    import spmv_decode_b200
+    from spmv_decode_b200 import _lib
+
+    pkg = Path(spmv_decode_b200.__file__).resolve().parent
+    for path in (pkg, Path(_lib.LIB_PATH).resolve()):
+        if ROOT not in path.parents:
+            raise RuntimeError(f"Foreign import: {path} is outside {ROOT}")
+
+
 def main():
     global _JSON_FD
     args = parse_args()
+    check_import_origin()
     # Libraries (NCCL's version banner, warnings) may write to file
     # descriptor 1: send it to stderr so stdout carries only the JSON line.
     sys.stdout.flush()

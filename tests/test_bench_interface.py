@@ -50,3 +50,17 @@ def test_reference_environment_sets_defaults(monkeypatch):
     monkeypatch.setenv("NM_M", "12")
     with pytest.raises(ValueError, match="Unsupported NM_M"):
         bench.parse_args()
+
+
+def test_import_origin_guard(monkeypatch):
+    """bench.py refuses a package or library from outside its own tree."""
+    from pathlib import Path
+
+    import pytest
+
+    from spmv_decode_b200 import _lib
+
+    bench.check_import_origin()
+    monkeypatch.setattr(_lib, "LIB_PATH", Path("/opt/elsewhere/libnmsparse_b200.so"))
+    with pytest.raises(RuntimeError, match="Foreign import"):
+        bench.check_import_origin()
