@@ -72,7 +72,8 @@ def env_defaults() -> dict:
     if "BENCH_WARMUP" in env:
         d["warmup"] = int(env["BENCH_WARMUP"])
     if "BENCH_REPEAT" in env or "BENCH_INNER" in env:
-        d["steps"] = int(env.get("BENCH_REPEAT", "30")) * int(env.get("BENCH_INNER", "10"))
+        d["inner"] = int(env.get("BENCH_INNER", "10"))
+        d["steps"] = int(env.get("BENCH_REPEAT", "30")) * d["inner"]
     if min(d["ctx"], d.get("warmup", 1), d.get("steps", 1)) < 1:
         raise ValueError("CTX, warmup, repeat, inner must be positive")
     return d
@@ -84,6 +85,8 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=env.get("steps", 1000))
     p.add_argument("--warmup", type=int, default=env.get("warmup", 50))
+    p.add_argument("--inner", type=int, default=env.get("inner", 10),
+                   help="replays per timed sample (the reference's BENCH_INNER); samples = steps // inner")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--model", default="llama-3.1-8b")
     p.add_argument("--nm", default=env.get("nm", "32:64"), help="N:M pattern, or 'dense'")
@@ -189,29 +192,47 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def time_graph(graph, stream, steps: int, warmup: int, world: int) -> float:
+def time_graph(graph, stream, steps: int, warmup: int, world: int, inner: int = 0) -> float:
     """Mean ms per replay over ``steps`` timed replays; max over ranks.
-    ``stream`` must be the current stream (the one replay() launches on)."""
+    ``stream`` must be the current stream (the one replay() launches on).
+    See time_graph_stats for the per-sample statistics."""
+    return time_graph_stats(graph, stream, steps, warmup, world, inner)["mean"]
+
+
+def time_graph_stats(graph, stream, steps: int, warmup: int, world: int, inner: int = 0) -> dict:
+    """Time ``steps`` replays as ``steps // inner`` samples of ``inner``
+    replays each (the reference's BENCH_REPEAT x BENCH_INNER,
+    benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:183-189): CUDA events
+    between samples on the replay stream, one device synchronize before and
+    after the whole timed region.  Returns the median, mean and stdev of the
+    per-sample ms per replay (the mean is over all replays); under
+    torchrun each is the max over ranks."""
     assert stream == torch.cuda.current_stream(), "time on the stream the graph replays on"
+    inner = max(1, min(inner or min(10, steps), steps))
+    reps = max(1, steps // inner)
+    steps = reps * inner
     for _ in range(warmup):
         graph.replay()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        graph.replay()
-    e1.record(stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    ev[0].record(stream)
+    for r in range(reps):
+        for _ in range(inner):
+            graph.replay()
+        ev[r + 1].record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    samples = [ev[r].elapsed_time(ev[r + 1]) / inner for r in range(reps)]
+    out = {"median": statistics.median(samples), "mean": ev[0].elapsed_time(ev[-1]) / steps,
+           "stdev": statistics.pstdev(samples) if reps > 1 else 0.0, "repeat": reps, "inner": inner,
+           "steps": steps}
     if world > 1:
         dist.barrier()
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        t = torch.tensor([out["median"], out["mean"], out["stdev"]], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return ms
+        out["median"], out["mean"], out["stdev"] = (float(v) for v in t.tolist())
+    return out
 
 
 def run_reference_arm(args, world: int, rank: int) -> None:
@@ -258,18 +279,18 @@ def emit(line: dict) -> None:
         os.write(_JSON_FD, data)
 
 
-def result_line(ctx: int, nm: str, mode: str, warmup: int, steps: int, ms: float) -> str:
+def result_line(ctx: int, nm: str, mode: str, warmup: int, st: dict) -> str:
     """The reference benchmark's summary line (benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:186-189),
-    the one its runner scripts parse (scripts/run_bench_qwen_32b_fp16.sh:215-219).  The timed
-    region is one sample (the mean over ``steps`` replays), so median = mean and stdev = 0."""
+    the one its runner scripts parse (scripts/run_bench_qwen_32b_fp16.sh:215-219): the median,
+    mean and stdev over ``repeat`` samples of ``inner`` replays each."""
     if nm == "dense":
         tag = "dense_float16"
     else:
         n, m = nm.split(":")
         tag = f"M={m}({n}:{m})"
     return (f"RESULT CTX={ctx} {tag} dtype=float16 actual_mode=b200_{mode} "
-            f"measurement=fixed_context_cuda_graph warmup={warmup} repeat=1 "
-            f"decode_ms_per_token={ms:.6f} mean={ms:.6f} stdev=0.000000")
+            f"measurement=fixed_context_cuda_graph warmup={warmup} repeat={st['repeat']} "
+            f"decode_ms_per_token={st['median']:.6f} mean={st['mean']:.6f} stdev={st['stdev']:.6f}")
 
 
 def check_import_origin() -> None:
@@ -283,6 +304,12 @@ def check_import_origin() -> None:
     for path in (pkg, Path(_lib.LIB_PATH).resolve()):
         if ROOT not in path.parents:
             raise RuntimeError(f"Foreign import: {path} is outside {ROOT}")
+    # ... and the library must have been built from the sources beside it.
+    from spmv_decode_b200 import build as _build
+
+    if _lib.source_hash() != _build.source_hash():
+        raise RuntimeError(f"stale library {_lib.LIB_PATH}: built from sources {_lib.source_hash()}, the tree has "
+                           f"{_build.source_hash()}; rebuild with `python -m spmv_decode_b200.build`")
 
 
 def main():
@@ -337,7 +364,8 @@ def main():
     graph = eng.capture(advance=False)
     stream = torch.cuda.current_stream(dev)
     clocks = ClockSampler(local_rank)
-    ms = time_graph(graph, stream, args.steps, args.warmup, world)
+    st = time_graph_stats(graph, stream, args.steps, args.warmup, world, args.inner)
+    ms = st["median"]
     clk = clocks.stop()
     assert torch.isfinite(eng.logits.float()).all(), "non-finite logits after replay"
     # Kernels of this library per step: one persistent kernel, or the plan's
@@ -481,8 +509,11 @@ def main():
     if rank == 0:
         pub = PUBLISHED.get((args.model, args.nm))
         line = {
-            "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": st["steps"],
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
+            "samples": {"repeat": st["repeat"], "inner": st["inner"], "median_ms": round(st["median"], 4),
+                        "mean_ms": round(st["mean"], 4), "stdev_ms": round(st["stdev"], 5),
+                        "note": "value = median of the samples (the reference's decode_ms_per_token)"},
             "vs_baseline": None if (pub is None or args.layers or args.vocab) else round(ms / pub[0], 4),
             "dtype": "f16 (fp32 accumulate)",
             "data": "synthetic: random-init weights N(0,0.02), KV cache N(0,0.02) (reference fixed-context protocol)",
@@ -496,7 +527,7 @@ def main():
             "gemv_roofline": gemv_roofline,
             "step_roofline": step_roofline,
             "cpu_baseline": cpu,
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": launches_per_step * st["steps"],
             "clocks": clk,
             "dense": dense,
             "baseline_published": None if pub is None else {"value": pub[0], "hardware": pub[1], "source": pub[2]},
@@ -505,7 +536,7 @@ def main():
         }
         emit(line)
         # stdout carries only the JSON line; the reference's RESULT line goes to stderr.
-        print(result_line(args.ctx, args.nm, engine_mode, args.warmup, args.steps, ms), file=sys.stderr, flush=True)
+        print(result_line(args.ctx, args.nm, engine_mode, args.warmup, st), file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier()
         tp.close()

@@ -43,6 +43,10 @@ enum nms_status {
 };
 
 int nms_abi_version(void);
+/* SHA-256 (hex) of the sources the library was built from (csrc/ and this
+ * header), so a caller can refuse a library that is older than its sources.
+ * No reference counterpart (the reference JIT-compiles its Triton kernel). */
+const char* nms_source_hash(void);
 const char* nms_last_error(void);
 const char* nms_status_name(int status);
 /* Number of SMs of the current device (also checks it is an sm_100 part). */
@@ -55,6 +59,13 @@ int nms_num_sms(int* out);
  * kernel skipped its work).  Synchronizes the current
  * device.  With clear != 0 the word is reset to 0. */
 int nms_device_error(int* code_out, int clear);
+/* Host-side abort request: sets the device error word to `code` (> 0).
+ * Kernels of this library that are inside a bounded wait (persistent-step
+ * grid barriers and tensor-parallel exchanges) give up at once and leave;
+ * a launch that starts while the word is set abandons its first barrier.
+ * The word stays set until nms_device_error(.., clear=1).  No reference
+ * counterpart: it lets a watchdog end a stuck step without a GPU fault. */
+int nms_device_error_set(int code);
 
 /* ---------------------------------------------------------------------------
  * Shared-mask N:M GEMV on the reference layout.
@@ -286,19 +297,34 @@ int nms_plan_launch(const nms_plan* plan, int32_t begin, int32_t end, void* stre
  * NMS_ERR_NOT_IMPLEMENTED, and the plan path is used.  nms_step_create
  * allocates the stage table and barrier/attention scratch once (device
  * memory, freed by nms_step_destroy); launches allocate nothing.  Barrier
- * waits are bounded (device error 3 on timeout).
+ * waits are bounded (device error 3 on timeout) and end early once the
+ * device error word is set; every CTA then still leaves through the exit
+ * path that zeroes the barrier words (the step's outputs are void).
  * ------------------------------------------------------------------------- */
 typedef struct nms_step nms_step;
 
 int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecords, nms_step** out);
 int nms_step_launch(const nms_step* step, void* stream);
 int nms_step_destroy(nms_step* step);
+/* Zero the step's barrier and attention arrival counters on `stream`.  Every
+ * CTA leaves through the same exit path, which resets them, even after an
+ * abandoned wait; a step that stopped inside an attention stage can still
+ * leave a head counter behind, so after a nonzero nms_device_error call this
+ * before the next launch (DecodeEngine.check_device does). */
+int nms_step_reset(const nms_step* step, void* stream);
 /* Stage count and CTAs of a persistent step. */
 int nms_step_info(const nms_step* step, int32_t* nstages, int32_t* grid);
 /* Optional timeline of later launches (NULL disables), in %globaltimer ns:
  * buf[0] = kernel start; buf[1 + s*(grid+1) + c] = when CTA c finished the
  * work of stage s; buf[1 + s*(grid+1) + grid] = when CTA 0 left the barrier
- * after stage s.  Needs 1 + nstages*(grid+1) uint64 entries (device memory). */
+ * after stage s.  Needs 1 + nstages*(grid+1) uint64 entries (device memory).
+ * With nstages*grid*8 more entries, a per-CTA detail (SM clock cycles of
+ * that CTA's clock64, for phase lengths within a stage) follows at
+ * buf[1 + nstages*(grid+1) + (s*grid + c)*8 + k]: k = 0 stage entry; GEMV:
+ * 1 input vector staged, 2 norm statistic done, 3 staged mask offsets / norm
+ * weights ready, 4 gathered vector built; attention: 4 first unit's q/k/v
+ * prepared; then 5 main work done (GEMV: weight items consumed; attention:
+ * partial state published), 6 stage finished; 7 unused. */
 int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity);
 
 /* ---------------------------------------------------------------------------

@@ -39,6 +39,9 @@ NMS_DTYPE_F32 = 2
 # Every exported symbol of include/nmsparse_b200.h (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
     "nms_abi_version",
+    "nms_source_hash",
+    "nms_device_error_set",
+    "nms_step_reset",
     "nms_last_error",
     "nms_status_name",
     "nms_num_sms",
@@ -163,6 +166,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     P, I32, I64 = c_void_p, c_i32, c_i64
     sig = {
         "nms_abi_version": (I32, []),
+        "nms_source_hash": (ctypes.c_char_p, []),
+        "nms_device_error_set": (I32, [I32]),
+        "nms_step_reset": (I32, [P, P]),
         "nms_last_error": (ctypes.c_char_p, []),
         "nms_status_name": (ctypes.c_char_p, [I32]),
         "nms_num_sms": (I32, [ctypes.POINTER(I32)]),
@@ -249,6 +255,11 @@ def device_error(clear: bool = True) -> int:
     v = c_i32(0)
     check(lib().nms_device_error(ctypes.byref(v), 1 if clear else 0), "nms_device_error")
     return int(v.value)
+
+
+def source_hash() -> str:
+    """SHA-256 of the sources the loaded library was built from."""
+    return lib().nms_source_hash().decode()
 
 
 def packed_row_stride(w: int) -> int:

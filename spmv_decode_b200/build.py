@@ -6,6 +6,7 @@ No JIT cache is involved, so the built file travels with the source tree.
 """
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -36,20 +37,47 @@ def sources() -> list[Path]:
     return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + [INCLUDE / "nmsparse_b200.h"])
 
 
-def needs_build() -> bool:
+def source_hash() -> str:
+    """SHA-256 over the library's sources (names and contents, in order); the
+    build embeds it and ``nms_source_hash()`` returns it."""
+    h = hashlib.sha256()
+    for p in sources():
+        h.update(p.name.encode() + b"\0" + p.read_bytes() + b"\0")
+    return h.hexdigest()
+
+
+def built_hash() -> str | None:
+    """The hash embedded in the built library, or None if there is none.
+    Read in a child process so this process never maps a library it may
+    replace a moment later."""
     if not OUT.exists():
-        return True
-    t = OUT.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in sources())
+        return None
+    code = ("import ctypes,sys; L=ctypes.CDLL(sys.argv[1]); f=L.nms_source_hash; "
+            "f.restype=ctypes.c_char_p; print(f().decode())")
+    res = subprocess.run([sys.executable, "-c", code, str(OUT)], capture_output=True, text=True)
+    return res.stdout.strip() if res.returncode == 0 else None
+
+
+def needs_build() -> bool:
+    return built_hash() != source_hash()
+
+
+def check_current() -> None:
+    """Raise if the built library was not built from the current sources."""
+    got, want = built_hash(), source_hash()
+    if got != want:
+        raise RuntimeError(f"{OUT} is stale (built from sources {got}, the tree has {want}); rebuild it with "
+                           "`python -m spmv_decode_b200.build`")
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile the library if any source is newer than the built file."""
+    """Compile the library unless it was built from exactly these sources."""
     if not force and not needs_build():
         return OUT
     OUT.parent.mkdir(parents=True, exist_ok=True)
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [_nvcc(), *NVCC_FLAGS, "-o", str(tmp), str(CSRC / "nms_lib.cu")]
+    cmd = [_nvcc(), *NVCC_FLAGS, f"-DNMS_SOURCE_HASH=\"{source_hash()}\"", "-o", str(tmp),
+           str(CSRC / "nms_lib.cu")]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)

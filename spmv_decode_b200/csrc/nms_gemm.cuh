@@ -337,6 +337,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ---- epilogue: TMEM lane (32 * warp + lane) holds tile row m0 + that ----
   const bool acc_ok = gemm_wait(&accum_bar, 0);
   tc_fence_after();
+  __syncthreads();  // s_abort, s_issued and s_consumed are final
+  if (threadIdx.x == 0 && s_abort) {
+    // A wait of the main loop gave up (kDevMmaTimeout recorded): let the
+    // tile copies still in flight land before the ring's shared memory is
+    // reused below (split-K receive buffer, output staging).  Each wait is
+    // bounded.  The cluster's output tile is then undefined -- it may be
+    // unwritten or hold partial sums -- and the caller must treat the
+    // launch's result as void.
+    for (int i = s_consumed; i < s_issued; ++i) {
+      if (!gemm_wait(&full_bar[i % p.stages], (uint32_t)(i / p.stages) & 1u)) break;
+    }
+  }
+  __syncthreads();
   const int row = warp * 32 + lane;
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
   const int nchunks = p.bn >> 4;
@@ -417,13 +430,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ---- teardown ----
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && s_abort) {
-    // Let copies still in flight land before the CTA's shared memory is
-    // released (each wait is bounded).
-    for (int i = s_consumed; i < s_issued; ++i) {
-      if (!gemm_wait(&full_bar[i % p.stages], (uint32_t)(i / p.stages) & 1u)) break;
-    }
-  }
+  // If the accumulator's commit never arrived, tensor-core work may still
+  // write TMEM: give it one more bounded wait before the columns are freed.
+  if (!acc_ok && warp == 2 && lane == 0) gemm_wait(&accum_bar, 0);
+  __syncwarp();
   if (warp == 2) tmem_dealloc(tmem, p.tmem_cols);
 }
 

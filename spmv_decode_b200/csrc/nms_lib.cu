@@ -709,12 +709,19 @@ struct nms_step {
   std::vector<nms::StepGemv> gemvs;    // host copy of the device GEMV stage table
   std::vector<int32_t> gemv_of_stage;  // stage -> GEMV ordinal (-1: attention)
   void* dev_mem = nullptr;  // stage tables | barrier words | attention partials | head counters
+  size_t bar_bytes = 0;     // barrier words at params.bar_count (arrivals, exits)
+  size_t cnt_bytes = 0;     // per-head attention arrival counters at params.attn_count
   nms::StepParams params;
 };
 
 extern "C" {
 
 int nms_abi_version(void) { return NMS_ABI_VERSION; }
+
+#ifndef NMS_SOURCE_HASH
+#define NMS_SOURCE_HASH "unknown"
+#endif
+const char* nms_source_hash(void) { return NMS_SOURCE_HASH; }
 
 const char* nms_last_error(void) { return g_last_error.c_str(); }
 
@@ -750,6 +757,13 @@ int nms_device_error(int* code_out, int clear) {
     e = cudaMemcpyToSymbol(nms::g_device_error, &zero, sizeof(int));
     if (e != cudaSuccess) return fail_cuda(e, "cudaMemcpyToSymbol(device error)");
   }
+  return NMS_OK;
+}
+
+int nms_device_error_set(int code) {
+  if (code <= 0) return fail(NMS_ERR_VALUE, "code must be positive (got %d); clear with nms_device_error", code);
+  cudaError_t e = cudaMemcpyToSymbol(nms::g_device_error, &code, sizeof(int));
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMemcpyToSymbol(device error)");
   return NMS_OK;
 }
 
@@ -1112,6 +1126,8 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
   P.trace = nullptr;
   P.pos = pos_ptr;
   P.tp_world = 1;
+  st->bar_bytes = 192;  // bar_count at +0, bar_exit at +128 (the head's local winner follows at +192)
+  st->cnt_bytes = total - cnt_off;
   st->gemvs = gemvs;
   st->gemv_of_stage.assign(kinds.size(), -1);
   for (size_t k = 0, g = 0; k < kinds.size(); ++k)
@@ -1246,16 +1262,28 @@ int nms_step_launch(const nms_step* step, void* stream) {
   return NMS_OK;
 }
 
+int nms_step_reset(const nms_step* step, void* stream) {
+  if (step == nullptr) return fail(NMS_ERR_VALUE, "step is null");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(step->params.bar_count, 0, step->bar_bytes, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(step->params.attn_count, 0, step->cnt_bytes, st);
+  if (e != cudaSuccess) return fail_cuda(e, "persistent step counter reset");
+  return NMS_OK;
+}
+
 int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity) {
   if (step == nullptr) return fail(NMS_ERR_VALUE, "step is null");
   if (buffer == nullptr) {
     step->params.trace = nullptr;
+    step->params.trace_detail = nullptr;
     return NMS_OK;
   }
   const int64_t need = 1 + (int64_t)step->nstages * (step->grid + 1);
   if (capacity < need) return fail(NMS_ERR_VALUE, "trace needs %lld entries, got %lld", (long long)need, (long long)capacity);
   if (!aligned(buffer, 8)) return fail(NMS_ERR_VALUE, "trace buffer must be 8-byte aligned");
   step->params.trace = static_cast<unsigned long long*>(buffer);
+  const int64_t detail = (int64_t)step->nstages * step->grid * nms::kTraceMarks;
+  step->params.trace_detail = capacity >= need + detail ? step->params.trace + need : nullptr;
   return NMS_OK;
 }
 

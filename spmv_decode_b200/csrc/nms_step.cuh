@@ -37,6 +37,7 @@ constexpr int kMaxSplits = 16;  // attention splits per KV head (cluster-size bo
 
 enum StageKind : int32_t { kStageGemv = 0, kStageAttn = 1 };
 constexpr int kMaxTp = 8;
+constexpr int kTraceMarks = 8;  // detail marks per stage and CTA
 
 struct StepGemv;
 struct ProdDesc;
@@ -57,6 +58,13 @@ struct StepParams {
   // trace[1 + s*(ncta+1) + c] = time CTA c finished stage s's work;
   // trace[1 + s*(ncta+1) + ncta] = time CTA 0 left the barrier after stage s.
   unsigned long long* trace;
+  // Optional per-CTA detail after the timeline (SM clock cycles, clock64):
+  // trace_detail[(s*ncta + c)*kTraceMarks + k], k = 0 stage entry; GEMV:
+  // 1 input vector staged, 2 norm statistic done, 3 staged masks / norm
+  // weights ready, 4 gathered vector built; attention: 4 first unit's q/k/v
+  // prepared; then 5 main work done (GEMV: weight items consumed;
+  // attention: partial state published), 6 stage finished.
+  unsigned long long* trace_detail;
   const int64_t* pos;       // token position of the step (all attention stages)
   // Tensor parallelism (tp_world > 1): exchange areas of every rank as
   // mapped in this process (values[nreduce][world][dim] of {fp32, tag}),
@@ -99,7 +107,7 @@ __device__ __forceinline__ void grid_arrive(unsigned* count) {
 }
 
 // Returns false (uniformly per CTA) when the wait ran past its limit
-// (kDevBarrierTimeout recorded).
+// (kDevBarrierTimeout recorded) or found the device error word set.
 __device__ __forceinline__ bool grid_wait(const unsigned* count, unsigned ncta, unsigned k) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
@@ -108,6 +116,12 @@ __device__ __forceinline__ bool grid_wait(const unsigned* count, unsigned ncta, 
     if (ld_acquire_u32(count) < target) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_u32(count) < target) {
+        // A recorded device error (a wait elsewhere gave up, or the host
+        // asked for an abort) ends the wait at once: the step is void.
+        if (*reinterpret_cast<volatile int*>(&g_device_error) != 0) {
+          ok = 0;
+          break;
+        }
         if (global_timer_ns() - t0 > kBarrierLimitNs) {
           set_device_error(kDevBarrierTimeout);
           ok = 0;
@@ -121,8 +135,11 @@ __device__ __forceinline__ bool grid_wait(const unsigned* count, unsigned ncta, 
   return s_ok != 0;
 }
 
-// Called once by every CTA as it leaves: the last one resets the barrier
-// counter (no CTA of this launch reads it any more).
+// Called once by every CTA as it leaves, on the normal path and after an
+// abandoned wait alike: the last one resets the barrier counter (no CTA of
+// this launch reads it any more) and, under tensor parallelism, counts the
+// step, so the next launch starts from zeroed counters and the exchange tags
+// stay in step with the peers'.
 __device__ __forceinline__ void step_exit(unsigned* count, unsigned* exit_count, unsigned ncta,
                                           unsigned long long* epoch) {
   __syncthreads();
@@ -449,10 +466,55 @@ __device__ __forceinline__ void gemv_pre_smem(const StepGemv& sg, unsigned ncta,
 // One GEMV stage after its barrier: input prologue (residual add, RMSNorm
 // statistic), gather, this warp's items from its ring (each consumed item
 // commits the warp's next copy), epilogue.
+// Stage the input vector (plus an addend, rounded to fp16 like the
+// reference's residual add) into shared memory with 16-byte L2 reads, U per
+// thread in flight at once; returns this thread's share of sum(x^2).
+template <int U, bool ADD>
+__device__ __forceinline__ float stage_input(const __half* x, const __half* x2, int K, __half* xs) {
+  const int K8 = K >> 3;
+  const uint4* xa = reinterpret_cast<const uint4*>(x);
+  const uint4* xb = reinterpret_cast<const uint4*>(x2);
+  float ss = 0.f;
+  for (int base = threadIdx.x; base < K8; base += U * kStepThreads) {
+    uint4 a[U], b[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i8 = base + u * kStepThreads;
+      a[u] = b[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (i8 < K8) {
+        a[u] = __ldcg(xa + i8);
+        if (ADD) b[u] = __ldcg(xb + i8);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i8 = base + u * kStepThreads;
+      if (i8 >= K8) break;
+      const __half* ah = reinterpret_cast<const __half*>(&a[u]);
+      const __half* bh = reinterpret_cast<const __half*>(&b[u]);
+      uint4 o;
+      __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const __half hv = ADD ? f2h(h2f(ah[e]) + h2f(bh[e])) : ah[e];
+        oh[e] = hv;
+        ss = fmaf(h2f(hv), h2f(hv), ss);
+      }
+      *reinterpret_cast<uint4*>(xs + (size_t)i8 * 8) = o;
+    }
+  }
+  return ss;
+}
+
+__device__ __forceinline__ void trace_at(unsigned long long* td, int k) {
+  if (td != nullptr && threadIdx.x == 0) td[k] = clock64();
+}
+
 template <int L, int D>
 __device__ __forceinline__ void gemv_stage(const StepParams& sp, const StepGemv& sg, const ProdDesc* descs, int ngemv,
                                            unsigned cta, unsigned ncta, unsigned char* act, Ring& R,
-                                           uint64_t* pre_bar, unsigned pre_uses, unsigned long long epoch) {
+                                           uint64_t* pre_bar, unsigned pre_uses, unsigned long long epoch,
+                                           unsigned long long* td) {
   constexpr int RG = kWarp / L, NT = kStepThreads, CB = 32 * L;
   const GemvParams& p = sg.g;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -471,22 +533,14 @@ __device__ __forceinline__ void gemv_stage(const StepParams& sp, const StepGemv&
   float ss = 0.f;
   if ((p.K & 7) == 0 && (reinterpret_cast<uintptr_t>(xsrc) & 15u) == 0 &&
       (!add || (reinterpret_cast<uintptr_t>(p.x2) & 15u) == 0)) {
-    for (int i8 = tid; i8 < p.K / 8; i8 += NT) {
-      const uint4 a = *reinterpret_cast<const uint4*>(xsrc + (size_t)i8 * 8);
-      uint4 b = make_uint4(0u, 0u, 0u, 0u);
-      if (add) b = *reinterpret_cast<const uint4*>(p.x2 + (size_t)i8 * 8);
-      const __half* ah = reinterpret_cast<const __half*>(&a);
-      const __half* bh = reinterpret_cast<const __half*>(&b);
-      uint4 o;
-      __half* oh = reinterpret_cast<__half*>(&o);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const __half hv = add ? f2h(h2f(ah[e]) + h2f(bh[e])) : ah[e];
-        oh[e] = hv;
-        ss = fmaf(h2f(hv), h2f(hv), ss);
-      }
-      *reinterpret_cast<uint4*>(s.xs + (size_t)i8 * 8) = o;
-    }
+    // The input (and residual addend) were written by other CTAs in the
+    // previous stage: read them from L2, every load of a thread issued
+    // before any is used (one round trip for K <= 32 * NT, or 16 * NT with
+    // an addend).
+    if (add)
+      ss = stage_input<2, true>(xsrc, p.x2, p.K, s.xs);
+    else
+      ss = stage_input<4, false>(xsrc, nullptr, p.K, s.xs);
   } else {
     for (int i = tid; i < p.K; i += NT) {
       float v = h2f(xsrc[i]);
@@ -495,36 +549,54 @@ __device__ __forceinline__ void gemv_stage(const StepParams& sp, const StepGemv&
       ss = fmaf(v, v, ss);
     }
   }
+  trace_at(td, 1);
   for (int v = tid; v < max_vrows; v += NT) s.acc[v] = 0.f;
   float rstd = 1.f;
   if (resid) {
+    // (its first block barrier also publishes the staged input)
     const float tot = block_reduce_sum(ss, s.red);
     rstd = 1.0f / sqrtf(tot / (float)p.K + p.eps);
+  } else {
+    __syncthreads();
   }
-  __syncthreads();
+  trace_at(td, 2);
   if (resid && p.resid_out != nullptr && cta == 0)
     for (int i = tid; i < p.K; i += NT) p.resid_out[i] = s.xs[i];
   if (pre_bulk(p)) mbar_wait_bounded(pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);  // staged masks / norm
-  // Gather (consecutive threads take consecutive kept positions: their mask
-  // group and so their shared-memory reads stay together).
+  trace_at(td, 3);
+  // Gather, four kept positions per thread and pass (one 4-byte read of
+  // their mask offsets, one 8-byte store); consecutive threads take
+  // consecutive positions, so their mask groups and shared-memory reads stay
+  // together.  Offsets past w are never used (the staged rows are 16-byte
+  // padded, so the 4-byte read stays inside them).
   const int n_shift = ((p.n & (p.n - 1)) == 0) ? __ffs(p.n) - 1 : -1;
+  const int wq = p.w_pad >> 2;
   for (int sx = 0; sx < nsegx; ++sx) {
     const uint8_t* idx = s.sidx + (size_t)sx * w_al;
     __half* xc = s.xc + (size_t)sx * p.w_pad;
-    for (int j = tid; j < p.w_pad; j += NT) {
-      __half val = __ushort_as_half((unsigned short)0);
-      if (j < p.w) {
-        const int grp = n_shift >= 0 ? (j >> n_shift) : j / p.n;
-        const int col = dense ? j : grp * p.m + (int)idx[j];
-        if (col < p.K) {
-          val = s.xs[col];
-          if (resid) val = f2h(h2f(f2h(h2f(val) * rstd)) * h2f(s.nw[col]));
+    for (int t = tid; t < wq; t += NT) {
+      const int j0 = t << 2;
+      const uint32_t ib = (!dense && j0 < p.w) ? *reinterpret_cast<const uint32_t*>(idx + j0) : 0u;
+      __align__(8) __half v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = j0 + e;
+        __half val = __ushort_as_half((unsigned short)0);
+        if (j < p.w) {
+          const int grp = n_shift >= 0 ? (j >> n_shift) : j / p.n;
+          const int col = dense ? j : grp * p.m + (int)((ib >> (8 * e)) & 0xffu);
+          if (col < p.K) {
+            val = s.xs[col];
+            if (resid) val = f2h(h2f(f2h(h2f(val) * rstd)) * h2f(s.nw[col]));
+          }
         }
+        v[e] = val;
       }
-      xc[j] = val;
+      *reinterpret_cast<uint2*>(xc + j0) = *reinterpret_cast<const uint2*>(v);
     }
   }
   __syncthreads();
+  trace_at(td, 4);
 
   if (q.t0 < q.t1) {
     int vg = q.t0 / q.cpr, c = q.t0 - vg * q.cpr;
@@ -562,6 +634,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams& sp, const StepGemv&
     }
   }
   __syncthreads();
+  trace_at(td, 5);
   if (sg.tp_send >= 0) {
     // Row-parallel shard: this CTA's fp32 partial rows go to slot
     // [tp_send][rank] of every rank's exchange area (over NVLink).
@@ -596,7 +669,7 @@ struct StepAttnSmem {
 };
 
 __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, int split, int kvh, StepAttnSmem& S,
-                                               float* part, unsigned* head_count) {
+                                               float* part, unsigned* head_count, unsigned long long* td) {
   constexpr int D = kAttnD, PT = kAttnTile, GM = kAttnMaxGroup, NT = kStepThreads;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = p.Hq / p.Hkv;
@@ -692,6 +765,7 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, 
     S.sl[tid] = 0.f;
   }
   __syncthreads();  // state initialised (an empty split publishes it unchanged)
+  trace_at(td, 4);
 
   for (int t0 = pb; t0 < pe; t0 += PT) {
     const int nt = min(PT, pe - t0);
@@ -782,6 +856,7 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, 
     }
   }
   __syncthreads();
+  trace_at(td, 5);
   if (!S.last) return;
   // Last split of this head: combine every split's state, read through L2.
   // The partial outputs a thread weights are loaded together with the
@@ -887,6 +962,55 @@ __device__ __forceinline__ void tp_head_token(const StepParams& sp, const __half
 }
 
 // ---------------------------------------------------------------------------
+// L2 residency of the step's small constant operands (mask offsets, RMSNorm
+// weights).  The weight rings keep tens of MB of requests queued in HBM, so
+// an operand that has to come from HBM at a stage boundary waits behind
+// them; with an evict-last prefetch at the start of every step these
+// operands stay in L2 while the weight stream (evict-normal) passes through.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void prefetch_l2_evict_last(const void* p) {
+  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+
+__device__ __forceinline__ void pin_small_operands(const StepParams& sp, unsigned cta, unsigned ncta) {
+  for (int gi = (int)cta; gi < sp.ngemv; gi += (int)ncta) {
+    const GemvParams& p = sp.gemv[gi].g;
+    const int nsegx = p.mode == kModePaired ? 2 : p.nseg;
+    int k = threadIdx.x;
+    if (p.seg[0].idx != nullptr) {
+      for (int sx = 0; sx < nsegx; ++sx) {
+        const int lines = (p.w + 127) >> 7;
+        for (; k < lines; k += kStepThreads) prefetch_l2_evict_last(p.seg[sx].idx + ((size_t)k << 7));
+        k -= lines;
+      }
+    }
+    if (p.prologue == kProResidNorm && p.norm_w != nullptr) {
+      const int lines = (p.K * 2 + 127) >> 7;
+      for (; k < lines; k += kStepThreads)
+        prefetch_l2_evict_last(reinterpret_cast<const char*>(p.norm_w) + ((size_t)k << 7));
+    }
+  }
+}
+
+// K/V rows [0, pos] of an attention stage pulled into L2 while the stage
+// before it runs (the attention's first loads are then L2 hits instead of
+// waiting behind the weight stream's queued requests).
+__device__ __forceinline__ void prefetch_kv_l2(const AttnParams& a, int pos, unsigned cta, unsigned ncta) {
+  if (threadIdx.x != 0 || pos < 0 || pos >= a.S_max) return;
+  constexpr uint32_t kChunk = 16384;
+  const uint32_t bytes = (uint32_t)(pos + 1) * kAttnD * 2;
+  const uint32_t per = (bytes + kChunk - 1) / kChunk;
+  const uint32_t total = 2u * (uint32_t)a.Hkv * per;
+  for (uint32_t c = cta; c < total; c += ncta) {
+    const uint32_t which = c / ((uint32_t)a.Hkv * per), rem = c - which * (uint32_t)a.Hkv * per;
+    const uint32_t h = rem / per, q = rem - h * per;
+    const char* base = reinterpret_cast<const char*>((which ? a.v_cache : a.k_cache) + (size_t)h * a.S_max * kAttnD);
+    const uint32_t off = q * kChunk, n = min(kChunk, bytes - off);
+    bulk_prefetch_l2(base + off, n);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // The persistent kernel (D: ring depth in items per warp).
 // ---------------------------------------------------------------------------
 constexpr int kGemvWords = (int)(sizeof(StepGemv) / 4);
@@ -897,12 +1021,12 @@ static_assert(kGemvWords <= kStepThreads && kAttnWords <= kStepThreads, "one par
 template <int D>
 __device__ __forceinline__ void run_gemv(const StepParams& sp, const StepGemv& sg, const ProdDesc* descs, int ngemv,
                                          unsigned cta, unsigned ncta, unsigned char* act, Ring& R, uint64_t* pre_bar,
-                                         unsigned pre_uses, unsigned long long epoch) {
+                                         unsigned pre_uses, unsigned long long epoch, unsigned long long* td) {
   switch (sg.lanes) {
-    case 32: gemv_stage<32, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
-    case 16: gemv_stage<16, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
-    case 8: gemv_stage<8, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
-    default: gemv_stage<4, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch); break;
+    case 32: gemv_stage<32, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch, td); break;
+    case 16: gemv_stage<16, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch, td); break;
+    case 8: gemv_stage<8, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch, td); break;
+    default: gemv_stage<4, D>(sp, sg, descs, ngemv, cta, ncta, act, R, pre_bar, pre_uses, epoch, td); break;
   }
 }
 
@@ -941,16 +1065,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   grid_dep_wait();
   if (sp.trace != nullptr && cta == 0 && tid == 0) sp.trace[0] = global_timer_ns();
+#if NMS_STEP_PF_SMALL
+  pin_small_operands(sp, cta, ncta);
+#endif
   // The token position is fixed for the whole step (the head advances it as
   // the last thing the step does): read it once.
   if (tid == 0) s_pos = (sp.pos != nullptr) ? (int)min((int64_t)0x7fffffff, max((int64_t)-1, *sp.pos)) : 0;
   if (sp.nstages > 0 && s_kind[0] == kStageGemv) gemv_pre_smem(s_g[0], ncta, act, &s_pre_bar, pre_uses);
   __syncthreads();
   int gn = 0, an = 0;  // ordinals of the next GEMV / attention stage
+  bool aborted = false;  // a grid barrier wait was abandoned (uniform per CTA)
   const unsigned long long epoch = (sp.tp_world > 1) ? *reinterpret_cast<volatile unsigned long long*>(sp.tp_epoch) : 0ull;
   for (int s = 0; s < sp.nstages; ++s) {
     int tp_j = -1;            // exchange point this stage feeds (tensor parallel)
     __half* tp_out = nullptr;
+    unsigned long long* td = sp.trace_detail ? sp.trace_detail + ((size_t)s * ncta + cta) * kTraceMarks : nullptr;
+    trace_at(td, 0);
+#if NMS_STEP_PF_KV
+    if (s + 1 < sp.nstages && s_kind[s + 1] == kStageAttn) prefetch_kv_l2(s_attn[an & 1], s_pos, cta, ncta);
+#endif
     if (s_kind[s] == kStageGemv) {
       // The next GEMV stage's parameters: loaded now, stored after this
       // stage into the slot GEMV gn-1 used.
@@ -959,7 +1092,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       if (more && tid < kGemvWords) stash = __ldg(reinterpret_cast<const uint32_t*>(sp.gemv + gn + 1) + tid);
       tp_j = s_g[gn & 1].tp_send;
       tp_out = s_g[gn & 1].g.out;
-      run_gemv<D>(sp, s_g[gn & 1], s_desc, sp.ngemv, cta, ncta, act, R, &s_pre_bar, pre_uses, epoch);
+      run_gemv<D>(sp, s_g[gn & 1], s_desc, sp.ngemv, cta, ncta, act, R, &s_pre_bar, pre_uses, epoch, td);
       if (more && tid < kGemvWords) reinterpret_cast<uint32_t*>(&s_g[(gn + 1) & 1])[tid] = stash;
       ++gn;
     } else {
@@ -970,7 +1103,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       const int units = a.Hkv * a.splits;
       StepAttnSmem& A = *reinterpret_cast<StepAttnSmem*>(act);
       for (int u = cta; u < units; u += ncta) {
-        attention_unit(a, s_pos, u % a.splits, u / a.splits, A, sp.attn_part, sp.attn_count);
+        attention_unit(a, s_pos, u % a.splits, u / a.splits, A, sp.attn_part, sp.attn_count, u == (int)cta ? td : nullptr);
         __syncthreads();
       }
       if (more && tid < kAttnWords) reinterpret_cast<uint32_t*>(&s_attn[(an + 1) & 1])[tid] = stash;
@@ -978,6 +1111,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
     unsigned long long* tr = sp.trace ? sp.trace + 1 + (size_t)s * (ncta + 1) : nullptr;
     if (tr != nullptr && tid == 0) tr[cta] = global_timer_ns();
+    trace_at(td, 6);
     if (tp_j >= 0) {
       // Tensor-parallel exchange point: the partial rows went out in the
       // epilogue carrying their arrival tags.  Each CTA sums its slice of the
@@ -993,10 +1127,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         grid_arrive(sp.bar_count);
         if (s_kind[s + 1] == kStageGemv) gemv_pre_smem(s_g[gn & 1], ncta, act, &s_pre_bar, pre_uses);
         if (!grid_wait(sp.bar_count, ncta, (unsigned)s)) {
-          asm volatile("cp.async.wait_all;" ::: "memory");
-          if (tid == 0 && pre_uses > 0u) mbar_wait_bounded(&s_pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);
-          __syncthreads();
-          return;
+          aborted = true;
+          break;
         }
       }
       if (tr != nullptr && cta == 0 && tid == 0) tr[ncta] = global_timer_ns();
@@ -1004,16 +1136,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       grid_arrive(sp.bar_count);  // includes __syncthreads: the stored parameters are visible
       if (s_kind[s + 1] == kStageGemv) gemv_pre_smem(s_g[gn & 1], ncta, act, &s_pre_bar, pre_uses);
       if (!grid_wait(sp.bar_count, ncta, (unsigned)s)) {
-        // No copy may land after exit.
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        if (tid == 0 && pre_uses > 0u) mbar_wait_bounded(&s_pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);
-        __syncthreads();
-        return;
+        aborted = true;
+        break;
       }
       if (tr != nullptr && cta == 0 && tid == 0) tr[ncta] = global_timer_ns();
     }
   }
-  if (sp.tp_world > 1 && sp.tp_head) {
+  if (aborted) {
+    // An abandoned wait: the staging of the next stage's masks / norm
+    // weights started before it may still be in flight; no copy may land
+    // after exit.  Then leave through step_exit like every other CTA.
+    if (tid == 0 && pre_uses > 0u) mbar_wait_bounded(&s_pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);
+    __syncthreads();
+  } else if (sp.tp_world > 1 && sp.tp_head) {
     // The head's last CTA wrote this rank's winner; every CTA has written its
     // logits: one grid barrier, then CTA 0 swaps candidates with the peers.
     grid_arrive(sp.bar_count);

@@ -39,6 +39,16 @@ from .nmsparse_linear import NmSparseLinear, sparse_prefill
 
 ARGMAX_CAPACITY = 2048
 
+# Device error codes (include/nmsparse_b200.h, nms_device_error).
+DEVICE_ERRORS = {
+    1: "bulk-copy wait timed out",
+    2: "token position outside the KV cache",
+    3: "grid barrier or tensor-parallel exchange wait timed out",
+    4: "weight-ring slot never refilled",
+    5: "weight-ring chunk does not fit its stage",
+    6: "prefill GEMM copy or tensor-core wait timed out",
+}
+
 
 def _linear_segment(lin) -> dict:
     """Segment description (packed weights, mask, rows, shape) of a linear."""
@@ -352,6 +362,23 @@ class DecodeEngine:
             with torch.cuda.stream(stream):
                 self.head_hook(advance)
 
+    def check_device(self) -> None:
+        """Raise ``RuntimeError`` if a kernel of this library recorded a
+        device error (a bounded wait that ran out, a position outside the KV
+        cache, or a host abort request), after the work enqueued so far has
+        finished.  The steps since the error are void.  The error word is
+        cleared and the persistent step's barrier and attention counters are
+        zeroed first, so the next step starts clean."""
+        code = _lib.device_error(clear=True)
+        if code == 0:
+            return
+        stream = torch.cuda.current_stream(self.device)
+        for h in self._steps.values():
+            _lib.check(_lib.lib().nms_step_reset(h, stream.cuda_stream), "nms_step_reset")
+        torch.cuda.synchronize(self.device)
+        raise RuntimeError(f"decode step failed on the device: error {code} ({DEVICE_ERRORS.get(code, 'unknown')}); "
+                           "the steps since the last check are void")
+
     def prefill(self, tokens, start_pos: int = 0) -> torch.Tensor:
         """Batched prefill: run ``tokens`` at positions ``start_pos ..`` through
         the model's own layers in one pass -- every N:M projection as one
@@ -431,11 +458,18 @@ class DecodeEngine:
         torch.cuda.synchronize(self.device)
         return g
 
-    def step_timeline(self, advance: bool = False, warmup: int = 2) -> dict:
+    def step_timeline(self, advance: bool = False, warmup: int = 2, detail: bool = False,
+                      sm_mhz: float = 1965.0) -> dict:
         """Run the persistent step once with its timeline enabled and return
         per-stage statistics in microseconds: work (previous barrier release to
         the slowest CTA's finish), imbalance (slowest - fastest CTA finish) and
-        barrier (slowest finish to release)."""
+        barrier (slowest finish to release).  With ``detail`` each stage also
+        gets ``marks_us``: for each detail mark 1..6 of the kernel's trace
+        (GEMV: input staged, norm statistic, masks ready, gathered vector,
+        items consumed, finish; attention: q/k/v prepared at mark 4,
+        published at 5, finish at 6) the mean over the CTAs that recorded it
+        of the time since stage entry, counted in SM clock cycles and
+        converted at ``sm_mhz`` (None where no CTA recorded it)."""
         if self.mode not in ("persistent", "persistent_tp"):
             raise RuntimeError("the timeline needs the persistent executor")
         L = _lib.lib()
@@ -443,7 +477,9 @@ class DecodeEngine:
         ns, grid = ctypes.c_int32(), ctypes.c_int32()
         _lib.check(L.nms_step_info(h, ctypes.byref(ns), ctypes.byref(grid)))
         n, g = int(ns.value), int(grid.value)
-        buf = torch.zeros(1 + n * (g + 1), dtype=torch.int64, device=self.device)
+        base = 1 + n * (g + 1)
+        marks = 8
+        buf = torch.zeros(base + (n * g * marks if detail else 0), dtype=torch.int64, device=self.device)
         for _ in range(warmup):
             self.step(advance=advance)
         _lib.check(L.nms_step_set_trace(h, buf.data_ptr(), buf.numel()))
@@ -452,14 +488,24 @@ class DecodeEngine:
         _lib.check(L.nms_step_set_trace(h, None, 0))
         t = buf.cpu().double()
         t0 = t[0].item()
-        rows = t[1:].view(n, g + 1)
+        rows = t[1:base].view(n, g + 1)
+        det = t[base:].view(n, g, marks) if detail else None
         stages = []
         prev = t0
         for s in range(n):
             fin = rows[s, :g]
             rel = rows[s, g].item() if s + 1 < n else fin.max().item()
-            stages.append({"work_us": (fin.max().item() - prev) / 1e3, "imbalance_us": (fin.max() - fin.min()).item() / 1e3,
-                           "barrier_us": (rel - fin.max().item()) / 1e3})
+            st = {"work_us": (fin.max().item() - prev) / 1e3, "imbalance_us": (fin.max() - fin.min()).item() / 1e3,
+                  "barrier_us": (rel - fin.max().item()) / 1e3}
+            if det is not None:
+                d = det[s]
+                e = d[:, 0]
+                mk = []
+                for k in range(1, 7):
+                    ok = d[:, k] > 0  # CTAs that recorded the mark (attention: CTAs with a unit)
+                    mk.append((d[ok, k] - e[ok]).mean().item() / sm_mhz if bool(ok.any()) else None)
+                st["marks_us"] = mk
+            stages.append(st)
             prev = rel
         return {"total_us": (prev - t0) / 1e3, "stages": stages}
 
@@ -500,38 +546,3 @@ class _CacheView(nn.Module):
         self.k[:, :, input_pos] = k_val
         self.v[:, :, input_pos] = v_val
         return self.k, self.v
-
-
-def smoke_step(dev: torch.device) -> None:
-    """Tiny fused decode step on ``dev`` checked against the CPU oracle (used
-    by __graft_entry__.smoke)."""
-    from .model import ModelArgs
-    from .nmsparse_linear import swap_to_nmsparse
-
-    cfg = ModelArgs(block_size=64, vocab_size=512, n_layer=2, n_head=2, dim=256, intermediate_size=512,
-                    n_local_heads=1)
-    torch.manual_seed(0)
-    with torch.device(dev):
-        model = Transformer(cfg)
-    with torch.no_grad():
-        model.tok_embeddings.weight.normal_(0, 0.02)
-        model.output.weight.normal_(0, 0.02)
-    model = model.to(torch.float16)
-    swap_to_nmsparse(model, 32, dev, seed=3)
-    eng = DecodeEngine(model, 32, history_len=32)
-    eng.token_in.fill_(7)
-    eng.pos.fill_(0)
-    eng.step()
-    torch.cuda.synchronize(dev)
-    from oracle.decode_oracle import OracleModel
-
-    om = OracleModel.from_transformer(model)
-    ref = om.step(7, 0)
-    got = eng.logits.float().cpu()
-    err = (got - ref.float()).abs().max().item()
-    scale = ref.float().abs().max().item()
-    if not (err <= 2e-2 * max(scale, 1e-3)):
-        raise AssertionError(f"smoke decode step mismatch: max abs err {err}, logit scale {scale}")
-    if int(eng.token_out.item()) != int(torch.argmax(eng.logits).item()):
-        raise AssertionError("smoke decode step: token_out is not the argmax of logits")
-    eng.close()

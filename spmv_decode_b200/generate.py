@@ -32,7 +32,9 @@ def decode_one_token(engine: DecodeEngine, token: int, input_pos: int) -> Tuple[
     engine.token_in.fill_(int(token))
     engine.pos.fill_(int(input_pos))
     engine.step(advance=False)
-    return int(engine.token_out.item()), engine.logits.clone()
+    tok = int(engine.token_out.item())
+    engine.check_device()
+    return tok, engine.logits.clone()
 
 
 class GraphDecoder:
@@ -64,6 +66,7 @@ class GraphDecoder:
             if keep_logits:
                 logits.append(e.logits.clone())
         torch.cuda.synchronize(e.device)
+        e.check_device()
         first = start_pos + n_prompt - 1
         toks = e.history[first: first + max_new_tokens].tolist()
         return toks, (torch.stack(logits) if keep_logits else None)

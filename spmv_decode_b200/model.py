@@ -1,3 +1,17 @@
+# Portions of this file (find_multiple, the ModelArgs fields, __post_init__,
+# from_name and the transformer_configs table, KVCache.update, RMSNorm,
+# apply_rope_scaling and the frequency lines of the RoPE table) follow
+# gpt-fast's model.py, which the reference ships as model.py under this notice:
+#
+#   Copyright (c) Meta Platforms, Inc. and affiliates.
+#   All rights reserved.
+#
+#   This source code is licensed under the license found in the
+#   LICENSE file in the root directory of this source tree.
+#
+# (gpt-fast is distributed under the BSD 3-Clause License.)  They are kept
+# alike on purpose: state dicts, configuration names and the bit-identical
+# fp16 RoPE table that decode parity needs depend on them.
 """Decoder model definitions for the decode engine (gpt-fast compatible).
 
 Mirrors the reference's model.py (ModelArgs, KVCache, Transformer,

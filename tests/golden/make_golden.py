@@ -1,9 +1,10 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in the build container only (it imports the reference from
-REFERENCE_ROOT, default /root/reference, which does not exist on GPU hosts):
+Run where the reference source tree is available (it imports the reference
+from the directory named by the REFERENCE_ROOT environment variable, which
+is required; GPU hosts do not have it):
 
-    python tests/golden/make_golden.py
+    REFERENCE_ROOT=<path to the reference checkout> python tests/golden/make_golden.py
 
 What it records, all produced by the reference's own code:
   packer.npz    -- _make_sparse (src/spmv/nmsparse_linear.py:14-33, shared-mask
@@ -36,7 +37,9 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+if "REFERENCE_ROOT" not in os.environ:
+    raise SystemExit("set REFERENCE_ROOT to the reference checkout (the directory holding triton_spmv.py)")
+REF = Path(os.environ["REFERENCE_ROOT"])
 
 os.environ["TRITON_INTERPRET"] = "1"
 os.environ["NM_KERNEL"] = "triton_ptx"

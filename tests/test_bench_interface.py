@@ -17,11 +17,13 @@ REF_RESULT = re.compile(
 
 
 def test_result_line_parses_like_the_reference():
-    line = bench.result_line(512, "32:64", "persistent", 50, 1000, 2.1735)
+    st = {"median": 2.1735, "mean": 2.1741, "stdev": 0.0012, "repeat": 100, "inner": 10, "steps": 1000}
+    line = bench.result_line(512, "32:64", "persistent", 50, st)
     ctx, tag, dtype, mode, med, mean, sd = REF_RESULT.findall(line)[-1]
     assert (ctx, tag, dtype, mode) == ("512", "M=64(32:64)", "float16", "b200_persistent")
-    assert float(med) == float(mean) == 2.1735 and float(sd) == 0.0
-    dense = bench.result_line(512, "dense", "persistent", 3, 10, 3.3)
+    assert (float(med), float(mean), float(sd)) == (2.1735, 2.1741, 0.0012)
+    assert "repeat=100" in line
+    dense = bench.result_line(512, "dense", "persistent", 3, dict(st, repeat=1))
     assert REF_RESULT.findall(dense)[-1][1] == "dense_float16"
 
 
@@ -40,7 +42,11 @@ def test_reference_environment_sets_defaults(monkeypatch):
     monkeypatch.setenv("BENCH_WARMUP", "7")
     monkeypatch.setenv("BENCH_REPEAT", "5")
     a = bench.parse_args()
-    assert (a.nm, a.ctx, a.warmup, a.steps) == ("8:16", 256, 7, 50)
+    assert (a.nm, a.ctx, a.warmup, a.steps, a.inner) == ("8:16", 256, 7, 50, 10)
+    monkeypatch.setenv("BENCH_INNER", "4")
+    a = bench.parse_args()
+    assert (a.steps, a.inner) == (20, 4)
+    monkeypatch.delenv("BENCH_INNER")
     monkeypatch.setattr(sys, "argv", ["bench.py", "--nm", "32:64", "--steps", "3"])
     a = bench.parse_args()
     assert (a.nm, a.steps) == ("32:64", 3)  # flags win

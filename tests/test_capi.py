@@ -194,3 +194,45 @@ def test_gemm_workspace_argument_validation(T, w_pad, h, msg):
     assert rc == _lib.NMS_ERR_VALUE and n.value == -1
     assert msg in _lib.lib().nms_last_error().decode()
     assert _lib.lib().nms_gemm_workspace_bytes(16, 2048, 4096, None) == _lib.NMS_ERR_VALUE
+
+
+def _call_noalloc(x=1, x2=None, norm=None, head=1, vocab=128, K=64, logits=1, token=1):
+    L = _lib.lib()
+    tok = ctypes.c_int64(0) if token else None
+    return L.nms_gemv_argmax_noalloc_f16(x, x2, norm, ctypes.c_float(1e-5), head, vocab, K, logits,
+                                         ctypes.byref(tok) if tok is not None else None, None)
+
+
+@pytest.mark.parametrize("kw, msg", [
+    (dict(x=None), "null pointer"),
+    (dict(head=None), "null pointer"),
+    (dict(logits=None), "null pointer"),
+    (dict(token=None), "null pointer"),
+    (dict(K=96), "multiple of 64"),
+    (dict(K=0), "multiple of 64"),
+    (dict(vocab=0), "out of range"),
+    (dict(vocab=(1 << 30) + 1), "out of range"),
+])
+def test_noalloc_head_argument_validation(kw, msg):
+    """nms_gemv_argmax_noalloc_f16 rejects bad arguments before any CUDA call."""
+    rc = _call_noalloc(**kw)
+    assert rc == _lib.NMS_ERR_VALUE
+    assert msg in _lib.lib().nms_last_error().decode()
+
+
+def test_device_error_set_rejects_non_positive_codes():
+    L = _lib.lib()
+    for code in (0, -3):
+        assert L.nms_device_error_set(code) == _lib.NMS_ERR_VALUE
+        assert "positive" in L.nms_last_error().decode()
+
+
+def test_step_reset_rejects_null():
+    assert _lib.lib().nms_step_reset(None, None) == _lib.NMS_ERR_VALUE
+
+
+def test_library_source_hash_matches_tree():
+    """The loaded library was built from the sources in this tree."""
+    from spmv_decode_b200 import build
+
+    assert _lib.source_hash() == build.source_hash()

@@ -128,18 +128,54 @@ def test_qwen3_06b_architecture_vs_oracle(cuda_device, mode):
     eng.close()
 
 
+# Every N:M ratio of BASELINE config 4 (the reference runner's NM_M loop,
+# scripts/run_bench_llama31_8b_triton_ptx_fp16.sh): the fused step's mask
+# staging and gather at G x N offsets from 2 up to 128 per group.
+RATIOS = [(2, 4), (4, 8), (8, 16), (16, 32), (32, 64), (64, 128), (128, 256)]
+
+
 @pytest.mark.parametrize("mode", MODES)
-def test_llama31_8b_width_vs_oracle(cuda_device, mode):
+@pytest.mark.parametrize("nm", RATIOS, ids=[f"{n}:{m}" for n, m in RATIOS])
+def test_llama31_8b_width_vs_oracle(cuda_device, nm, mode):
     """Llama-3.1-8B widths (hidden 4096, 32/8 heads, SwiGLU 14336, untied 128256
-    head, RoPE theta 5e5 with 3.1 scaling) at 2 layers, 32:64; 64 greedy steps."""
+    head, RoPE theta 5e5 with 3.1 scaling) at 2 layers, every N:M ratio; 64
+    greedy steps."""
     args = ModelArgs.from_name("llama-3.1-8b")
     args.n_layer = 2
-    model = build_model(args, nm=(32, 64), device=cuda_device, seed=3, init="reference")
+    model = build_model(args, nm=nm, device=cuda_device, seed=3, init="reference")
     prompt = torch.randint(0, 128256, (16,), generator=torch.Generator().manual_seed(6)).tolist()
     eng = DecodeEngine(model, 128, history_len=128, mode=mode)
+    assert eng.mode == mode
     om = OracleModel.from_transformer(model, max_seq=128)
     toks, agree, ties, worst = _teacher_forced_check(eng, om, prompt, 64)
     assert agree + ties == 64 and agree >= 60
+    assert _lib.device_error() == 0
+    eng.close()
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_qwen3_32b_width_vs_oracle(cuda_device, mode):
+    """Qwen3-32B widths (the reference runs it through HF
+    Qwen3ForCausalLM, benchmarks/bench_qwen_3_32b_fp16_fixed_ptx.py:331-355):
+    hidden 5120, 64 query / 8 KV heads (a GQA group of 8, the attention's
+    widest), q/k RMSNorm, SwiGLU 25600, untied 151936 head, 16:32, at 2
+    layers, with non-unit norm weights; 64 greedy steps teacher-forced."""
+    args = ModelArgs.from_name("qwen3-32b")
+    args.n_layer = 2
+    model = build_model(args, nm=(16, 32), device=cuda_device, seed=7, init="reference")
+    g = torch.Generator(device=cuda_device).manual_seed(8)
+    with torch.no_grad():
+        for mod in model.modules():
+            if mod.__class__.__name__ == "RMSNorm":
+                mod.weight.copy_((1.0 + 0.2 * torch.randn(mod.weight.shape, generator=g, device=cuda_device))
+                                 .to(torch.float16))
+    prompt = torch.randint(0, 151936, (16,), generator=torch.Generator().manual_seed(9)).tolist()
+    eng = DecodeEngine(model, 128, history_len=128, mode=mode)
+    assert eng.mode == mode
+    om = OracleModel.from_transformer(model, max_seq=128)
+    toks, agree, ties, worst = _teacher_forced_check(eng, om, prompt, 64)
+    assert agree + ties == 64 and agree >= 60
+    assert _lib.device_error() == 0
     eng.close()
 
 
@@ -200,4 +236,28 @@ def test_auto_mode_is_persistent(cuda_device):
                                   intermediate_size=384), nm=(16, 32), device=cuda_device, seed=5)
     eng = DecodeEngine(model, 32, history_len=32, mode="auto")
     assert eng.mode == "persistent"
+    eng.close()
+
+
+def test_abort_request_voids_step_and_engine_recovers(cuda_device):
+    """A host-side abort request (nms_device_error_set, the injection a
+    watchdog would use -- no GPU fault) makes the step's bounded waits give
+    up; the engine raises after its sync, clears the word, zeroes the step's
+    barrier and attention counters, and the next step is bit-identical to
+    one from a fresh engine."""
+    model = build_model(ModelArgs(block_size=64, vocab_size=1024, n_layer=2, n_head=4, n_local_heads=2, dim=512,
+                                  intermediate_size=1024), nm=(8, 16), device=cuda_device, seed=12)
+    eng = DecodeEngine(model, 64, history_len=64, mode="persistent")
+    assert _lib.device_error() == 0
+    ref_tok, ref_logits = decode_one_token(eng, 5, 0)
+    for _ in range(2):  # twice: the recovery itself must leave clean state behind
+        eng.reset()
+        _lib.check(_lib.lib().nms_device_error_set(3))
+        with pytest.raises(RuntimeError, match="error 3"):
+            decode_one_token(eng, 5, 0)
+        assert _lib.device_error(clear=False) == 0
+        eng.reset()
+        tok, logits = decode_one_token(eng, 5, 0)
+        assert tok == ref_tok
+        assert torch.equal(logits, ref_logits)
     eng.close()
