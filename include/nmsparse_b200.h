@@ -304,6 +304,20 @@ int nms_plan_launch(const nms_plan* plan, int32_t begin, int32_t end, void* stre
 typedef struct nms_step nms_step;
 
 int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecords, nms_step** out);
+/* The same step as a dataflow kernel without grid barriers: each stage's
+ * output travels as tagged words ({fp16 value, tag} in 32 bits; per-CTA
+ * fp32 partials as {value, tag} in 64 bits) that are their own arrival
+ * signal; the o- and down-projection epilogues own their rows of the
+ * residual stream and scatter them straight into the next stage's N:M
+ * compressed input (inverse tables built here from mat_index); the RMSNorm
+ * statistic arrives as per-CTA partials added in CTA order.  The routing is
+ * derived from the records by pointer identity (the x, x2, resid_out and
+ * out vectors of the decode step, as DecodeEngine builds it); a plan it
+ * cannot route returns NMS_ERR_NOT_IMPLEMENTED and nms_step_create applies.
+ * Not combinable with nms_step_set_tp.  Waits are bounded (device error 3)
+ * and end once the device error word is set.  No reference counterpart
+ * (replaces the same compiled + graph-captured decode_one_token). */
+int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t nrecords, nms_step** out);
 int nms_step_launch(const nms_step* step, void* stream);
 int nms_step_destroy(nms_step* step);
 /* Zero the step's barrier and attention arrival counters on `stream`.  Every

@@ -66,6 +66,7 @@ EXPORTED_SYMBOLS = (
     "nms_plan_size",
     "nms_plan_launch",
     "nms_step_create",
+    "nms_step_create_flow",
     "nms_step_launch",
     "nms_step_destroy",
     "nms_step_info",
@@ -193,6 +194,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "nms_plan_size": (I32, [P, ctypes.POINTER(I32)]),
         "nms_plan_launch": (I32, [P, I32, I32, P]),
         "nms_step_create": (I32, [P, ctypes.POINTER(I32), I32, ctypes.POINTER(P)]),
+        "nms_step_create_flow": (I32, [P, ctypes.POINTER(I32), I32, ctypes.POINTER(P)]),
         "nms_step_launch": (I32, [P, P]),
         "nms_step_destroy": (I32, [P]),
         "nms_step_info": (I32, [P, ctypes.POINTER(I32), ctypes.POINTER(I32)]),

@@ -19,7 +19,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <type_traits>
 #include <string>
 #include <utility>
 #include <vector>
@@ -31,6 +33,7 @@
 #include "nms_gemm.cuh"
 #include "nms_gemv.cuh"
 #include "nms_step.cuh"
+#include "nms_flow.cuh"
 
 namespace {
 
@@ -103,7 +106,9 @@ int device_info(const DeviceInfo** out) {
     d.max_smem_optin = (size_t)smem - static_max;
     d.step_smem_max = (size_t)smem;
     for (const void* k : {(const void*)nms::decode_step_kernel<nms::kStepDepthHi>,
-                          (const void*)nms::decode_step_kernel<nms::kStepDepthLo>}) {
+                          (const void*)nms::decode_step_kernel<nms::kStepDepthLo>,
+                          (const void*)nms::decode_flow_kernel<nms::kStepDepthHi>,
+                          (const void*)nms::decode_flow_kernel<nms::kStepDepthLo>}) {
       cudaFuncAttributes fa;
       e = cudaFuncGetAttributes(&fa, k);
       if (e != cudaSuccess) return fail_cuda(e, "cudaFuncGetAttributes(decode_step_kernel)");
@@ -711,6 +716,8 @@ struct nms_step {
   void* dev_mem = nullptr;  // stage tables | barrier words | attention partials | head counters
   size_t bar_bytes = 0;     // barrier words at params.bar_count (arrivals, exits)
   size_t cnt_bytes = 0;     // per-head attention arrival counters at params.attn_count
+  bool flow = false;        // dataflow kernel (decode_flow_kernel) instead of the barrier kernel
+  nms::FlowParams fparams;  // flow: kernel parameters (tables and words live in dev_mem)
   nms::StepParams params;
 };
 
@@ -1136,6 +1143,379 @@ int nms_step_create(const nms_plan* plan, const int32_t* records, int32_t nrecor
   return NMS_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Dataflow persistent step (decode_flow_kernel).  The routing of every
+// stage's output is derived from the plan records by pointer identity:
+//   * a residual + RMSNorm GEMV N (x, x2, norm, resid_out) makes the GEMV
+//     whose output is x2 a residual producer: it reads the residual words
+//     that stand for x, writes resid_new (standing for N's resid_out), its
+//     sum-of-squares partials, and scatters resid_new into N's compressed
+//     inputs (one inverse table per mask segment of N);
+//   * a plain GEMV N reads the output of the attention stage or SwiGLU GEMV
+//     that writes its x, scattered the same way;
+//   * an attention stage reads the words of the GEMV that writes its qkv;
+//   * the first stage may read the embedding row (x_token) and gathers it
+//     by mask itself.
+// Anything else is refused with NMS_ERR_NOT_IMPLEMENTED (the caller then
+// uses nms_step_create).  Device memory, one block: [static tables (inverse
+// maps, mask-gathered norm weights) | stage tables, words, partials].
+// ---------------------------------------------------------------------------
+}  // extern "C"
+
+namespace {
+
+struct FlowArena {
+  size_t static_end = 0, end = 0;
+  std::vector<unsigned char> init;  // host image of the static region
+  size_t take_static(size_t bytes) {
+    const size_t off = nms::align_up_sz(static_end, 256);
+    static_end = off + bytes;
+    init.resize(static_end, 0);
+    return off;
+  }
+  size_t take_dyn(size_t bytes) {
+    const size_t off = nms::align_up_sz(end, 256);
+    end = off + bytes;
+    return off;
+  }
+};
+
+enum : int { kOwnNone = 0, kOwnGemv = 1, kOwnAttn = 2 };
+struct FlowOwner {
+  int kind = kOwnNone, index = -1;
+};
+
+// Offsets stand in for device pointers until the block is allocated; the
+// top bit marks an offset into the dynamic region, +1 keeps offset 0 apart
+// from nullptr.
+constexpr uintptr_t kFlowDynBit = (uintptr_t)1 << 62;
+template <typename T>
+T* flow_off(size_t off, bool dynamic) {
+  return reinterpret_cast<T*>((uintptr_t)(off + 1) | (dynamic ? kFlowDynBit : 0));
+}
+
+int read_mask(const nms::GemvParams& g, int sx, std::vector<uint8_t>* idx) {
+  idx->resize((size_t)g.w);
+  cudaError_t e = cudaMemcpy(idx->data(), g.seg[sx].idx, (size_t)g.w, cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? NMS_OK : fail_cuda(e, "reading mat_index");
+}
+
+}  // namespace
+
+extern "C" {
+
+int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t nrecords, nms_step** out) {
+  if (plan == nullptr || out == nullptr || records == nullptr) return fail(NMS_ERR_VALUE, "null argument");
+  const int32_t n = (int32_t)plan->recs.size();
+  if (nrecords < 1) return fail(NMS_ERR_VALUE, "no records");
+  for (int32_t k = 0; k < nrecords; ++k)
+    if (records[k] < 0 || records[k] >= n) return fail(NMS_ERR_VALUE, "record %d outside plan of %d", records[k], n);
+  const DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const int grid = dev->num_sms;
+  constexpr int NT = nms::kStepThreads;
+
+  std::vector<int32_t> kinds;
+  std::vector<nms::FlowGemv> fg;
+  std::vector<nms::ProdDesc> descs;
+  std::vector<nms::FlowAttn> fa;
+  FlowArena ar;
+  std::map<const void*, FlowOwner> out_owner;
+  std::map<const void*, uint32_t*> resid_of;  // plain residual vector -> words standing for it
+  std::vector<uint32_t*> natural_of_gemv;      // natural-order output words of a GEMV (nullptr: none)
+  std::vector<uint32_t*> natural_of_attn;
+  size_t act = sizeof(nms::StepAttnSmem);
+  const int64_t* pos_ptr = nullptr;
+
+  for (int32_t k = 0; k < nrecords; ++k) {
+    const int32_t i = records[k];
+    const LaunchRec& r = plan->recs[i];
+    if (r.kind == LaunchRec::kGemvPacked) {
+      const int gi = (int)fg.size();
+      nms::FlowGemv f;
+      memset(&f, 0, sizeof(f));
+      nms::StepGemv& sg = f.sg;
+      sg.g = r.gp;
+      sg.lanes = nms::ring_lanes(sg.g.w_pad);
+      sg.tp_send = sg.tp_recv = -1;
+      const int RG = 32 / sg.lanes;
+      sg.g.row_groups = (sg.g.rows_total + RG - 1) / RG;
+      const nms::GemvParams& g = sg.g;
+      if (g.epilogue == nms::kEpiArgmax && (g.amax_val == nullptr || grid > r.amax_capacity))
+        return fail(NMS_ERR_VALUE, "record %d: argmax scratch holds %d partials, the step needs %d", i,
+                    r.amax_capacity, grid);
+      const bool paired = g.mode == nms::kModePaired;
+      const int nsegx = paired ? 2 : g.nseg;
+      const bool dense = g.seg[0].idx == nullptr;
+      const bool norm = g.prologue == nms::kProResidNorm;
+      const int max_vrows = (paired ? 2 : 1) * ((g.row_groups + grid - 1) / grid) * RG;
+      f.out_mode = -1;
+      f.in_mode = nms::kFlowInTagged;
+      if (dense && (g.w != g.K || g.w_pad != g.K))
+        return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: dense stage with w != K", i);
+      // This stage's compressed inputs and the producer's scatter targets;
+      // `natural`: the producer's natural-order words (allocated here when a
+      // dense input needs them).
+      auto route_inputs = [&](int prod_kind, int prod_index) -> int {
+        uint32_t*& natural = prod_kind == kOwnGemv ? natural_of_gemv[prod_index] : natural_of_attn[prod_index];
+        for (int sx = 0; sx < nsegx; ++sx) {
+          if (dense) {
+            if (natural == nullptr) natural = flow_off<uint32_t>(ar.take_dyn((size_t)g.K * 4), true);
+            f.xc_in[sx] = natural;
+            continue;
+          }
+          std::vector<uint8_t> idx;
+          int rc2 = read_mask(g, sx, &idx);
+          if (rc2) return rc2;
+          const size_t inv_off = ar.take_static((size_t)g.K * 4);
+          int32_t* inv = reinterpret_cast<int32_t*>(ar.init.data() + inv_off);
+          for (int c = 0; c < g.K; ++c) inv[c] = -1;
+          for (int j = 0; j < g.w; ++j) {
+            const int col = (j / g.n) * g.m + (int)idx[j];
+            if ((int)idx[j] >= g.m || col >= g.K || inv[col] != -1)
+              return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: mask segment %d is not an N:M selection", i, sx);
+            inv[col] = j;
+          }
+          uint32_t* xc = flow_off<uint32_t>(ar.take_dyn((size_t)g.w_pad * 4), true);
+          f.xc_in[sx] = xc;
+          const int32_t* invp = flow_off<const int32_t>(inv_off, false);
+          if (prod_kind == kOwnGemv) {
+            nms::FlowGemv& P = fg[prod_index];
+            if (P.nscat >= nms::kFlowMaxScat)
+              return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: too many scatter targets", i);
+            P.scat_dst[P.nscat] = xc;
+            P.scat_inv[P.nscat] = invp;
+            ++P.nscat;
+          } else {
+            nms::FlowAttn& A = fa[prod_index];
+            if (A.y_dst != nullptr)
+              return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: attention output feeds two masks", i);
+            A.y_dst = xc;
+            A.y_inv = invp;
+          }
+        }
+        return NMS_OK;
+      };
+      if (g.x_token != nullptr) {
+        if (k != 0) return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: only the first stage may read the embedding", i);
+        f.in_mode = nms::kFlowInGather;
+        if (g.resid_out != nullptr) {
+          f.gather_resid = flow_off<uint32_t>(ar.take_dyn((size_t)g.K * 4), true);
+          resid_of[g.resid_out] = f.gather_resid;
+        }
+      } else if (norm) {
+        auto it = out_owner.find(g.x2);
+        auto rx = resid_of.find(g.x);
+        if (g.x2 == nullptr || it == out_owner.end() || it->second.kind != kOwnGemv || rx == resid_of.end())
+          return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: residual inputs are not produced inside the step", i);
+        nms::FlowGemv& P = fg[it->second.index];
+        if (P.out_mode != -1 || P.sg.g.epilogue != nms::kEpiStore || P.sg.g.mode == nms::kModePaired ||
+            P.sg.g.rows_total != g.K)
+          return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: residual producer is not a plain %d-row GEMV", i, g.K);
+        P.out_mode = nms::kFlowOutResid;
+        P.resid_old = rx->second;
+        uint32_t* words = flow_off<uint32_t>(ar.take_dyn((size_t)g.K * 4), true);
+        natural_of_gemv[it->second.index] = words;
+        if (g.resid_out != nullptr) resid_of[g.resid_out] = words;
+        P.ssq_out = flow_off<unsigned long long>(ar.take_dyn((size_t)grid * 8), true);
+        f.ssq_in = P.ssq_out;
+        // Norm weights gathered by mask (dense: the weights themselves).
+        std::vector<uint16_t> nw((size_t)g.K);
+        cudaError_t e = cudaMemcpy(nw.data(), g.norm_w, (size_t)g.K * 2, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return fail_cuda(e, "reading norm weights");
+        const size_t nwc_off = ar.take_static((size_t)nsegx * g.w_pad * 2);
+        for (int sx = 0; sx < nsegx; ++sx) {
+          uint16_t* dst = reinterpret_cast<uint16_t*>(ar.init.data() + nwc_off) + (size_t)sx * g.w_pad;
+          if (dense) {
+            for (int j = 0; j < g.K; ++j) dst[j] = nw[j];
+          } else {
+            std::vector<uint8_t> idx;
+            rc = read_mask(g, sx, &idx);
+            if (rc) return rc;
+            for (int j = 0; j < g.w; ++j) {
+              const int col = (j / g.n) * g.m + (int)idx[j];
+              if (col < g.K) dst[j] = nw[col];
+            }
+          }
+        }
+        f.nwc = flow_off<const __half>(nwc_off, false);
+        rc = route_inputs(kOwnGemv, it->second.index);
+        if (rc) return rc;
+      } else {
+        auto it = out_owner.find(g.x);
+        if (it == out_owner.end())
+          return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: input is not produced inside the step", i);
+        if (it->second.kind == kOwnGemv) {
+          nms::FlowGemv& P = fg[it->second.index];
+          if (P.out_mode != -1 || P.sg.g.epilogue != nms::kEpiSwiGLU)
+            return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: a plain input must come from a SwiGLU GEMV", i);
+          P.out_mode = nms::kFlowOutAct;
+        }
+        rc = route_inputs(it->second.kind, it->second.index);
+        if (rc) return rc;
+      }
+      if (g.epilogue == nms::kEpiArgmax) f.out_mode = nms::kFlowOutArgmax;
+      size_t a0, a1, a2, a3, a4, a5, a6;
+      const size_t need_sm = nms::flow_gemv_layout(g.K, g.w, g.w_pad, nsegx, max_vrows, norm,
+                                                   f.in_mode == nms::kFlowInGather, &a0, &a1, &a2, &a3, &a4, &a5, &a6);
+      if (need_sm > act) act = need_sm;
+      if (((g.row_groups + grid - 1) / grid) * RG > NT && g.epilogue != nms::kEpiArgmax)
+        return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: more than %d output rows per CTA", i, NT);
+      nms::ProdDesc pd;
+      memset(&pd, 0, sizeof(pd));
+      for (int q = 0; q < g.nseg; ++q) {
+        pd.w[q] = g.seg[q].w;
+        pd.row_start[q] = g.seg[q].row_start;
+      }
+      pd.rows_total = g.rows_total;
+      pd.row_groups = g.row_groups;
+      pd.w_pad = g.w_pad;
+      pd.nseg = (int16_t)g.nseg;
+      pd.paired = paired ? 1 : 0;
+      pd.lanes = (int8_t)sg.lanes;
+      kinds.push_back(nms::kStageGemv);
+      fg.push_back(f);
+      descs.push_back(pd);
+      natural_of_gemv.push_back(nullptr);
+      if (g.epilogue != nms::kEpiArgmax) out_owner[g.out] = FlowOwner{kOwnGemv, gi};
+    } else if (r.kind == LaunchRec::kAttention) {
+      const int ai = (int)fa.size();
+      nms::FlowAttn a;
+      memset(&a, 0, sizeof(a));
+      a.a = r.ap;
+      const int units = a.a.Hkv * a.a.splits;
+      if (a.a.splits > nms::kMaxSplits || units > grid)
+        return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: %d attention units for %d CTAs", i, units, grid);
+      if (pos_ptr == nullptr) pos_ptr = a.a.pos;
+      if (a.a.pos != pos_ptr) return fail(NMS_ERR_VALUE, "record %d: attention stages must share one position", i);
+      auto it = out_owner.find(a.a.qkv);
+      const int qkv_rows = (a.a.Hq + 2 * a.a.Hkv) * nms::kAttnD;
+      if (it == out_owner.end() || it->second.kind != kOwnGemv)
+        return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: q/k/v are not produced inside the step", i);
+      nms::FlowGemv& Q = fg[it->second.index];
+      if (Q.out_mode != -1 || Q.sg.g.epilogue != nms::kEpiStore || Q.sg.g.rows_total != qkv_rows)
+        return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: the q/k/v producer is not a plain %d-row GEMV", i, qkv_rows);
+      Q.out_mode = nms::kFlowOutWords;
+      uint32_t* words = flow_off<uint32_t>(ar.take_dyn((size_t)qkv_rows * 4), true);
+      natural_of_gemv[it->second.index] = words;
+      a.qkv_in = words;
+      const int G = a.a.Hq / a.a.Hkv;
+      a.part = flow_off<unsigned long long>(ar.take_dyn((size_t)units * G * (nms::kAttnD + 2) * 8), true);
+      kinds.push_back(nms::kStageAttn);
+      fa.push_back(a);
+      natural_of_attn.push_back(nullptr);
+      out_owner[a.a.y] = FlowOwner{kOwnAttn, ai};
+    } else {
+      return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: only GEMV and attention launches run in a persistent step", i);
+    }
+  }
+  for (size_t gi = 0; gi < fg.size(); ++gi) {
+    if (fg[gi].out_mode == -1)
+      return fail(NMS_ERR_NOT_IMPLEMENTED, "GEMV stage %zu: its output is not consumed inside the step", gi);
+    fg[gi].out_words = natural_of_gemv[gi];
+  }
+  for (size_t ai = 0; ai < fa.size(); ++ai) fa[ai].y_words = natural_of_attn[ai];
+  if (fg.empty() || kinds.back() != nms::kStageGemv || fg.back().out_mode != nms::kFlowOutArgmax)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "the step must end with the argmax head");
+
+  // Shared memory: [rings][working set][stream descriptors][stage kinds].
+  act = nms::align_up_sz(act, 128);
+  const size_t tail_bytes = descs.size() * sizeof(nms::ProdDesc) + nms::align_up_sz(kinds.size() * 4, 16);
+  const size_t ring_unit = (size_t)nms::kStepWarps * nms::kRingItemBytes;
+  int depth = 0;
+  for (int d : {nms::kStepDepthHi, nms::kStepDepthLo})
+    if (depth == 0 && (size_t)d * ring_unit + act + tail_bytes <= dev->step_smem_max) depth = d;
+  if (depth == 0)
+    return fail(NMS_ERR_NOT_IMPLEMENTED, "flow step: a %zu-byte working set leaves no room for the weight rings", act);
+
+  const size_t kind_off = ar.take_dyn(kinds.size() * 4);
+  const size_t gemv_off = ar.take_dyn(fg.size() * sizeof(nms::FlowGemv));
+  const size_t desc_off = ar.take_dyn(descs.size() * sizeof(nms::ProdDesc));
+  const size_t attn_off = ar.take_dyn(std::max<size_t>(1, fa.size()) * sizeof(nms::FlowAttn));
+  const size_t ctl_off = ar.take_dyn(256);  // exit counter at +0, spare word at +64, epoch at +128
+  const size_t static_bytes = nms::align_up_sz(ar.static_end, 256);
+  const size_t total = static_bytes + ar.end;
+
+  nms_step* st = new (std::nothrow) nms_step();
+  if (st == nullptr) return fail(NMS_ERR_CUDA, "out of host memory");
+  cudaError_t e = cudaGetDevice(&st->device);
+  if (e == cudaSuccess) e = cudaMalloc(&st->dev_mem, total);
+  if (e == cudaSuccess) e = cudaMemset(st->dev_mem, 0, total);
+  unsigned char* base = static_cast<unsigned char*>(st->dev_mem);
+  auto dyn_addr = [&](size_t off) { return base + static_bytes + off; };
+  auto patch = [&](auto*& ptr) {
+    if (ptr == nullptr) return;
+    const uintptr_t v = reinterpret_cast<uintptr_t>(ptr);
+    const size_t off = (size_t)((v & ~kFlowDynBit) - 1);
+    unsigned char* a = (v & kFlowDynBit) ? base + static_bytes + off : base + off;
+    ptr = reinterpret_cast<std::remove_reference_t<decltype(ptr)>>(a);
+  };
+  for (nms::FlowGemv& f : fg) {
+    for (int q = 0; q < nms::kMaxSegs; ++q) patch(f.xc_in[q]);
+    patch(f.nwc);
+    patch(f.ssq_in);
+    patch(f.gather_resid);
+    patch(f.out_words);
+    patch(f.resid_old);
+    patch(f.ssq_out);
+    for (int q = 0; q < nms::kFlowMaxScat; ++q) {
+      patch(f.scat_dst[q]);
+      patch(f.scat_inv[q]);
+    }
+  }
+  for (nms::FlowAttn& a : fa) {
+    patch(a.qkv_in);
+    patch(a.part);
+    patch(a.y_words);
+    patch(a.y_dst);
+    patch(a.y_inv);
+  }
+  if (e == cudaSuccess && ar.static_end > 0) e = cudaMemcpy(base, ar.init.data(), ar.static_end, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dyn_addr(kind_off), kinds.data(), kinds.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(dyn_addr(gemv_off), fg.data(), fg.size() * sizeof(nms::FlowGemv), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(dyn_addr(desc_off), descs.data(), descs.size() * sizeof(nms::ProdDesc), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && !fa.empty())
+    e = cudaMemcpy(dyn_addr(attn_off), fa.data(), fa.size() * sizeof(nms::FlowAttn), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    if (st->dev_mem) cudaFree(st->dev_mem);
+    delete st;
+    return fail_cuda(e, "flow step set-up");
+  }
+  st->flow = true;
+  st->nstages = (int)kinds.size();
+  st->grid = grid;
+  st->depth = depth;
+  st->smem = (size_t)depth * ring_unit + act + tail_bytes;
+  nms::FlowParams& F = st->fparams;
+  memset(&F, 0, sizeof(F));
+  F.kind = reinterpret_cast<const int32_t*>(dyn_addr(kind_off));
+  F.gemv = reinterpret_cast<const nms::FlowGemv*>(dyn_addr(gemv_off));
+  F.desc = reinterpret_cast<const nms::ProdDesc*>(dyn_addr(desc_off));
+  F.attn = reinterpret_cast<const nms::FlowAttn*>(dyn_addr(attn_off));
+  F.nstages = st->nstages;
+  F.ngemv = (int32_t)fg.size();
+  F.nattn = (int32_t)fa.size();
+  F.ring_bytes = (int32_t)((size_t)depth * ring_unit);
+  F.act_bytes = (int32_t)act;
+  F.exit_count = reinterpret_cast<unsigned*>(dyn_addr(ctl_off));
+  F.spare = reinterpret_cast<unsigned*>(dyn_addr(ctl_off) + 64);
+  F.epoch = reinterpret_cast<unsigned long long*>(dyn_addr(ctl_off) + 128);
+  F.pos = pos_ptr;
+  memset(&st->params, 0, sizeof(st->params));
+  // nms_step_reset zeroes the exit counter and the spare word; the epoch
+  // keeps counting (tags stay unique).
+  st->params.bar_count = F.exit_count;
+  st->params.attn_count = F.spare;
+  st->bar_bytes = 4;
+  st->cnt_bytes = 4;
+  st->gemv_of_stage.assign(kinds.size(), -1);
+  *out = st;
+  return NMS_OK;
+}
+
 int64_t nms_tp_area_bytes(int32_t nreduce, int32_t world, int32_t dim) {
   if (nreduce < 1 || world < 1 || dim < 1) return -1;
   return 256 + (int64_t)(nreduce + 1) * world * (dim < 2 ? 2 : dim) * 8;  // + the head's candidate point
@@ -1184,6 +1564,7 @@ int nms_step_set_tp(nms_step* step, const int32_t* reduce_stages, int32_t nreduc
     return fail(NMS_ERR_VALUE, "world=%d rank=%d (2 <= world <= %d)", cfg->world, cfg->rank, NMS_MAX_TP);
   if (nreduce < 1 || cfg->dim < 2) return fail(NMS_ERR_VALUE, "nreduce=%d dim=%d", nreduce, cfg->dim);
   if (step->params.tp_world > 1) return fail(NMS_ERR_VALUE, "tensor parallelism is already set for this step");
+  if (step->flow) return fail(NMS_ERR_NOT_IMPLEMENTED, "tensor parallelism runs on the barrier step (nms_step_create)");
   for (int r = 0; r < cfg->world; ++r)
     if (cfg->area[r] == nullptr || !aligned(cfg->area[r], 256)) return fail(NMS_ERR_VALUE, "area %d missing or unaligned", r);
   std::vector<nms::StepGemv> g = step->gemvs;
@@ -1254,6 +1635,14 @@ int nms_step_set_tp(nms_step* step, const int32_t* reduce_stages, int32_t nreduc
 
 int nms_step_launch(const nms_step* step, void* stream) {
   if (step == nullptr) return fail(NMS_ERR_VALUE, "step is null");
+  if (step->flow) {
+    cudaError_t e = launch_ex2(step->depth == nms::kStepDepthHi ? nms::decode_flow_kernel<nms::kStepDepthHi>
+                                                               : nms::decode_flow_kernel<nms::kStepDepthLo>,
+                               dim3(step->grid), dim3(nms::kStepThreads), step->smem,
+                               static_cast<cudaStream_t>(stream), false, dim3(1, 1, 1), true, step->fparams);
+    if (e != cudaSuccess) return fail_cuda(e, "decode_flow_kernel launch");
+    return NMS_OK;
+  }
   cudaError_t e = launch_ex2(step->depth == nms::kStepDepthHi ? nms::decode_step_kernel<nms::kStepDepthHi>
                                                              : nms::decode_step_kernel<nms::kStepDepthLo>,
                              dim3(step->grid), dim3(nms::kStepThreads), step->smem, static_cast<cudaStream_t>(stream),
@@ -1276,6 +1665,8 @@ int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity) {
   if (buffer == nullptr) {
     step->params.trace = nullptr;
     step->params.trace_detail = nullptr;
+    step->fparams.trace = nullptr;
+    step->fparams.trace_detail = nullptr;
     return NMS_OK;
   }
   const int64_t need = 1 + (int64_t)step->nstages * (step->grid + 1);
@@ -1284,6 +1675,8 @@ int nms_step_set_trace(nms_step* step, void* buffer, int64_t capacity) {
   step->params.trace = static_cast<unsigned long long*>(buffer);
   const int64_t detail = (int64_t)step->nstages * step->grid * nms::kTraceMarks;
   step->params.trace_detail = capacity >= need + detail ? step->params.trace + need : nullptr;
+  step->fparams.trace = step->params.trace;
+  step->fparams.trace_detail = step->params.trace_detail;
   return NMS_OK;
 }
 

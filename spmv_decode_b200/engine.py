@@ -38,6 +38,9 @@ from .model import Transformer, precompute_rope_table
 from .nmsparse_linear import NmSparseLinear, sparse_prefill
 
 ARGMAX_CAPACITY = 2048
+# Persistent kernels tried before the barrier kernel in modes "auto" and
+# "persistent" (the dataflow kernel, when enabled).
+FLOW_DEFAULT: List[str] = []
 
 # Device error codes (include/nmsparse_b200.h, nms_device_error).
 DEVICE_ERRORS = {
@@ -89,7 +92,7 @@ class DecodeEngine:
         # Tensor parallelism: after the (non-advancing) local head, head_hook(advance)
         # turns the rank's argmax into the global greedy token.
         self.head_hook = head_hook
-        if mode not in ("auto", "persistent", "plan"):
+        if mode not in ("auto", "persistent", "flow", "barrier", "plan"):
             raise ValueError(f"unknown mode {mode!r}")
         self.tp_rank, self.tp_size = tp_rank, tp_size
         Hq, Hkv = local_heads if local_heads is not None else (c.n_head, c.n_local_heads)
@@ -140,20 +143,30 @@ class DecodeEngine:
             self._steps = {}
             self.mode = "plan"
             if mode != "plan" and allreduce is None and head_hook is None:
-                try:
-                    fixed = list(range(self._head_index)) + [self._head_index]
-                    adv = list(range(self._head_index)) + [self._head_index + 1]
-                    for key, recs in ((False, fixed), (True, adv)):
-                        arr = (ctypes.c_int32 * len(recs))(*recs)
-                        h = ctypes.c_void_p()
-                        _lib.check(_lib.lib().nms_step_create(self._plan, arr, len(recs), ctypes.byref(h)),
-                                   "nms_step_create")
-                        self._steps[key] = h
-                    self.mode = "persistent"
-                except NotImplementedError:
-                    if mode == "persistent":
-                        raise
-                    self._destroy_steps()
+                # Persistent executors, in order of preference: the dataflow
+                # kernel (no grid barriers), then the barrier kernel.
+                kinds = {"auto": FLOW_DEFAULT + ["barrier"], "persistent": FLOW_DEFAULT + ["barrier"],
+                         "flow": ["flow"], "barrier": ["barrier"]}[mode]
+                for kind in kinds:
+                    try:
+                        self._create_steps(kind)
+                        self.mode = "flow" if kind == "flow" else "persistent"
+                        break
+                    except NotImplementedError:
+                        self._destroy_steps()
+                        if kind == kinds[-1] and mode != "auto":
+                            raise
+
+    def _create_steps(self, kind: str) -> None:
+        """Persistent steps (fixed and advancing head) of the given kernel kind."""
+        create = _lib.lib().nms_step_create_flow if kind == "flow" else _lib.lib().nms_step_create
+        fixed = list(range(self._head_index)) + [self._head_index]
+        adv = list(range(self._head_index)) + [self._head_index + 1]
+        for key, recs in ((False, fixed), (True, adv)):
+            arr = (ctypes.c_int32 * len(recs))(*recs)
+            h = ctypes.c_void_p()
+            _lib.check(create(self._plan, arr, len(recs), ctypes.byref(h)), f"nms_step_create ({kind})")
+            self._steps[key] = h
 
     # ------------------------------------------------------------------ build
     def _h(self, t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -338,7 +351,7 @@ class DecodeEngine:
         writes logits and token_out (and with ``advance`` also token_in,
         history[pos] and pos += 1)."""
         stream = stream or torch.cuda.current_stream(self.device)
-        if self.mode == "persistent":
+        if self.mode in ("persistent", "flow"):
             _lib.check(_lib.lib().nms_step_launch(self._steps[advance], stream.cuda_stream), "nms_step_launch")
             return
         if self.mode == "persistent_tp":
@@ -375,6 +388,7 @@ class DecodeEngine:
         stream = torch.cuda.current_stream(self.device)
         for h in self._steps.values():
             _lib.check(_lib.lib().nms_step_reset(h, stream.cuda_stream), "nms_step_reset")
+        self.amax_counter.zero_()  # the head's arrival counter, if the step stopped inside it
         torch.cuda.synchronize(self.device)
         raise RuntimeError(f"decode step failed on the device: error {code} ({DEVICE_ERRORS.get(code, 'unknown')}); "
                            "the steps since the last check are void")
@@ -470,8 +484,8 @@ class DecodeEngine:
         published at 5, finish at 6) the mean over the CTAs that recorded it
         of the time since stage entry, counted in SM clock cycles and
         converted at ``sm_mhz`` (None where no CTA recorded it)."""
-        if self.mode not in ("persistent", "persistent_tp"):
-            raise RuntimeError("the timeline needs the persistent executor")
+        if self.mode not in ("persistent", "persistent_tp", "flow"):
+            raise RuntimeError("the timeline needs a persistent executor")
         L = _lib.lib()
         h = self._steps[advance]
         ns, grid = ctypes.c_int32(), ctypes.c_int32()
@@ -494,7 +508,9 @@ class DecodeEngine:
         prev = t0
         for s in range(n):
             fin = rows[s, :g]
-            rel = rows[s, g].item() if s + 1 < n else fin.max().item()
+            # The flow kernel has no barrier: a stage "releases" when its
+            # slowest CTA finishes.
+            rel = rows[s, g].item() if (s + 1 < n and rows[s, g].item() > 0) else fin.max().item()
             st = {"work_us": (fin.max().item() - prev) / 1e3, "imbalance_us": (fin.max() - fin.min()).item() / 1e3,
                   "barrier_us": (rel - fin.max().item()) / 1e3}
             if det is not None:

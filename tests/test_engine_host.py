@@ -24,7 +24,8 @@ class _FakeLib:
 
 
 def _fake_engine():
-    return types.SimpleNamespace(_steps={False: "step-fixed", True: "step-adv"}, device=torch.device("cpu"))
+    return types.SimpleNamespace(_steps={False: "step-fixed", True: "step-adv"}, device=torch.device("cpu"),
+                                 amax_counter=torch.ones(1, dtype=torch.int32))
 
 
 def test_check_device_raises_clears_and_resets(monkeypatch):
@@ -46,6 +47,7 @@ def test_check_device_raises_clears_and_resets(monkeypatch):
         DecodeEngine.check_device(eng)
     assert word["v"] == 0
     assert sorted(fake.resets) == [("step-adv", 77), ("step-fixed", 77)]
+    assert int(eng.amax_counter.item()) == 0  # the head's arrival counter starts clean too
     # Clean word: no exception, no reset.
     DecodeEngine.check_device(eng)
     assert len(fake.resets) == 2
