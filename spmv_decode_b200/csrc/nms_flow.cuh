@@ -113,6 +113,43 @@ __device__ __noinline__ bool poll_f32t(const unsigned long long* p, uint32_t tag
   return true;
 }
 
+// Stage completion hints.  A producer CTA bumps its stage's counter with a
+// fire-and-forget relaxed add after its stores; one thread of a consumer CTA
+// waits (bounded) for the count of this step before the CTA reads its words,
+// so a CTA that is early does not have all its threads spinning on L2.  The
+// counter is only a hint: the tags stay the proof that a word is of this
+// step (a word seen early is polled by itself).  Counters are zeroed by the
+// last CTA to leave the kernel.
+__device__ __forceinline__ void red_rlx_add_u32(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_rlx_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Whole CTA: returns false (uniformly) if the wait gave up.
+__device__ __forceinline__ bool flow_wait_done(const unsigned* cnt, unsigned need, int* s_fail) {
+  if (cnt != nullptr && threadIdx.x == 0 && ld_rlx_u32(cnt) < need) {
+    const uint64_t t0 = global_timer_ns();
+    while (ld_rlx_u32(cnt) < need) {
+      if (*reinterpret_cast<volatile int*>(&g_device_error) != 0) {
+        atomicExch(s_fail, 1);
+        break;
+      }
+      if (global_timer_ns() - t0 > kPollLimitNs) {
+        set_device_error(kDevBarrierTimeout);
+        atomicExch(s_fail, 1);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  return *reinterpret_cast<volatile int*>(s_fail) == 0;
+}
+
 // Read a tagged fp32 word, polling until it carries tag32.
 __device__ __forceinline__ float get_f32t(const unsigned long long* p, uint32_t tag32, bool& ok) {
   unsigned long long w = ld_rlx_b64(p);
@@ -137,7 +174,10 @@ constexpr int kFlowMaxScat = 4;
 
 struct FlowGemv {
   StepGemv sg;
-  int32_t in_mode, out_mode, nscat, pad_;
+  int32_t in_mode, out_mode, nscat;
+  uint32_t done_need;                 // increments of done_in per step
+  const unsigned* done_in;            // the input producer's completion counter (nullptr: none)
+  unsigned* done_out;                 // this stage's completion counter
   // kFlowInTagged: gathered vector sx is the word array xc_in[sx] (position
   // j < w; positions >= w are zero), norm stages also take the producer's
   // per-CTA sum-of-squares partials and the norm weights gathered by mask.
@@ -156,6 +196,9 @@ struct FlowGemv {
 
 struct FlowAttn {
   AttnParams a;
+  uint32_t done_need, pad_;
+  const unsigned* done_in;      // the q/k/v stage's completion counter
+  unsigned* done_out;           // bumped by each combining unit
   const uint32_t* qkv_in;       // [(Hq + 2 Hkv) * D] words of the q/k/v stage
   unsigned long long* part;     // [units][G][D + 2] partial softmax states (m, l, o)
   uint32_t* y_words;            // natural-order y words [Hq * D] (dense o-projection) or nullptr
@@ -171,6 +214,8 @@ struct FlowParams {
   int32_t nstages, ngemv, nattn;
   int32_t ring_bytes, act_bytes;
   unsigned* exit_count;           // CTAs that have left (reset by the last)
+  unsigned* counters;             // [ncounters] stage completion hints (zeroed by the last CTA to leave)
+  int32_t ncounters, pad_;
   unsigned* spare;                // zeroed word (step_exit's barrier-counter slot)
   unsigned long long* epoch;      // completed steps (tags)
   unsigned long long* trace;      // as StepParams::trace (no barrier release times: 0)
@@ -382,6 +427,7 @@ __device__ __forceinline__ bool flow_gemv_stage(const FlowGemv& fg, const ProdDe
     }
   } else {
     // -------- tagged input: poll the compressed words (and partials) -----
+    if (!flow_wait_done(fg.done_in, fg.done_need, s_fail)) return false;
     const int wq = p.w_pad >> 2;
     for (int t = tid; t < nsegx * wq; t += NT) {
       const int sx = t / wq, j0 = (t - sx * wq) << 2;
@@ -514,6 +560,7 @@ __device__ __forceinline__ bool flow_gemv_stage(const FlowGemv& fg, const ProdDe
     gemv_epilogue<NT>(p, s.acc, q.g0, q.ng, RG, cta, ncta);
   }
   __syncthreads();
+  if (tid == 0 && fg.done_out != nullptr) red_rlx_add_u32(fg.done_out, 1u);
   return *reinterpret_cast<volatile int*>(s_fail) == 0;
 }
 
@@ -591,6 +638,7 @@ __device__ __noinline__ bool flow_attention_unit(const FlowAttn& fa, int pos_in,
   // before the q/k/v words are polled.
   if (pb < pe) load_tile(pb);
 
+  if (!flow_wait_done(fa.done_in, fa.done_need, s_fail)) return false;
   bool ok = true;
   // Four consecutive dims per lane: one 16-byte read of the words.
   auto head_words = [&](int row0, float (&v)[4]) {
@@ -832,6 +880,8 @@ __device__ __noinline__ bool flow_attention_unit(const FlowAttn& fa, int pos_in,
       }
     }
   }
+  __syncthreads();
+  if (tid == 0 && fa.done_out != nullptr) red_rlx_add_u32(fa.done_out, 1u);
   return *reinterpret_cast<volatile int*>(s_fail) == 0;
 }
 
@@ -924,7 +974,23 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_flow_kernel(const __gr
   asm volatile("cp.async.wait_all;" ::: "memory");
   if (aborted && tid == 0 && pre_uses > 0u) mbar_wait_bounded(&s_pre_bar, (pre_uses - 1u) & 1u, kPreWaitLimitNs);
   __syncthreads();
-  step_exit(fp.spare, fp.exit_count, ncta, fp.epoch);
+  // Leave: the last CTA zeroes the completion counters (no CTA of this
+  // launch reads them any more), then counts the step.
+  __shared__ int s_last;
+  if (tid == 0) {
+    __threadfence();
+    s_last = (atomicAdd(fp.exit_count, 1u) == ncta - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (s_last) {
+    for (int i = tid; i < fp.ncounters; i += kStepThreads) fp.counters[i] = 0u;
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      atomicExch(fp.exit_count, 0u);
+      atomicAdd(fp.epoch, 1ull);
+    }
+  }
   grid_dep_launch_dependents();
 }
 

@@ -1227,6 +1227,7 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
   std::vector<uint32_t*> natural_of_attn;
   size_t act = sizeof(nms::StepAttnSmem);
   const int64_t* pos_ptr = nullptr;
+  int nstage_counter = 0;  // completion counters, one per stage (offsets patched once the block exists)
 
   for (int32_t k = 0; k < nrecords; ++k) {
     const int32_t i = records[k];
@@ -1252,6 +1253,7 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
       const int max_vrows = (paired ? 2 : 1) * ((g.row_groups + grid - 1) / grid) * RG;
       f.out_mode = -1;
       f.in_mode = nms::kFlowInTagged;
+      f.done_out = flow_off<unsigned>((size_t)(nstage_counter++) * 4, true);  // offset into the counter block, patched below
       if (dense && (g.w != g.K || g.w_pad != g.K))
         return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: dense stage with w != K", i);
       // This stage's compressed inputs and the producer's scatter targets;
@@ -1320,6 +1322,8 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
         if (g.resid_out != nullptr) resid_of[g.resid_out] = words;
         P.ssq_out = flow_off<unsigned long long>(ar.take_dyn((size_t)grid * 8), true);
         f.ssq_in = P.ssq_out;
+        f.done_in = P.done_out;
+        f.done_need = (uint32_t)grid;
         // Norm weights gathered by mask (dense: the weights themselves).
         std::vector<uint16_t> nw((size_t)g.K);
         cudaError_t e = cudaMemcpy(nw.data(), g.norm_w, (size_t)g.K * 2, cudaMemcpyDeviceToHost);
@@ -1351,6 +1355,11 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
           if (P.out_mode != -1 || P.sg.g.epilogue != nms::kEpiSwiGLU)
             return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: a plain input must come from a SwiGLU GEMV", i);
           P.out_mode = nms::kFlowOutAct;
+          f.done_in = P.done_out;
+          f.done_need = (uint32_t)grid;
+        } else {
+          f.done_in = fa[it->second.index].done_out;
+          f.done_need = (uint32_t)fa[it->second.index].a.Hkv;  // one combining unit per KV head
         }
         rc = route_inputs(it->second.kind, it->second.index);
         if (rc) return rc;
@@ -1397,6 +1406,9 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
       if (Q.out_mode != -1 || Q.sg.g.epilogue != nms::kEpiStore || Q.sg.g.rows_total != qkv_rows)
         return fail(NMS_ERR_NOT_IMPLEMENTED, "record %d: the q/k/v producer is not a plain %d-row GEMV", i, qkv_rows);
       Q.out_mode = nms::kFlowOutWords;
+      a.done_in = Q.done_out;
+      a.done_need = (uint32_t)grid;
+      a.done_out = flow_off<unsigned>((size_t)(nstage_counter++) * 4, true);
       uint32_t* words = flow_off<uint32_t>(ar.take_dyn((size_t)qkv_rows * 4), true);
       natural_of_gemv[it->second.index] = words;
       a.qkv_in = words;
@@ -1434,6 +1446,7 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
   const size_t desc_off = ar.take_dyn(descs.size() * sizeof(nms::ProdDesc));
   const size_t attn_off = ar.take_dyn(std::max<size_t>(1, fa.size()) * sizeof(nms::FlowAttn));
   const size_t ctl_off = ar.take_dyn(256);  // exit counter at +0, spare word at +64, epoch at +128
+  const size_t cnt_off = ar.take_dyn((size_t)std::max(1, nstage_counter) * 4);
   const size_t static_bytes = nms::align_up_sz(ar.static_end, 256);
   const size_t total = static_bytes + ar.end;
 
@@ -1451,6 +1464,20 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
     unsigned char* a = (v & kFlowDynBit) ? base + static_bytes + off : base + off;
     ptr = reinterpret_cast<std::remove_reference_t<decltype(ptr)>>(a);
   };
+  // Completion counters were numbered, not placed: rebase them onto their block.
+  auto patch_cnt = [&](auto*& ptr) {
+    if (ptr == nullptr) return;
+    const size_t idx = (size_t)(((reinterpret_cast<uintptr_t>(ptr) & ~kFlowDynBit) - 1) / 4);
+    ptr = reinterpret_cast<std::remove_reference_t<decltype(ptr)>>(dyn_addr(cnt_off) + idx * 4);
+  };
+  for (nms::FlowGemv& f : fg) {
+    patch_cnt(f.done_in);
+    patch_cnt(f.done_out);
+  }
+  for (nms::FlowAttn& a : fa) {
+    patch_cnt(a.done_in);
+    patch_cnt(a.done_out);
+  }
   for (nms::FlowGemv& f : fg) {
     for (int q = 0; q < nms::kMaxSegs; ++q) patch(f.xc_in[q]);
     patch(f.nwc);
@@ -1501,6 +1528,8 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
   F.ring_bytes = (int32_t)((size_t)depth * ring_unit);
   F.act_bytes = (int32_t)act;
   F.exit_count = reinterpret_cast<unsigned*>(dyn_addr(ctl_off));
+  F.counters = reinterpret_cast<unsigned*>(dyn_addr(cnt_off));
+  F.ncounters = nstage_counter;
   F.spare = reinterpret_cast<unsigned*>(dyn_addr(ctl_off) + 64);
   F.epoch = reinterpret_cast<unsigned long long*>(dyn_addr(ctl_off) + 128);
   F.pos = pos_ptr;
@@ -1508,9 +1537,9 @@ int nms_step_create_flow(const nms_plan* plan, const int32_t* records, int32_t n
   // nms_step_reset zeroes the exit counter and the spare word; the epoch
   // keeps counting (tags stay unique).
   st->params.bar_count = F.exit_count;
-  st->params.attn_count = F.spare;
+  st->params.attn_count = F.counters;
   st->bar_bytes = 4;
-  st->cnt_bytes = 4;
+  st->cnt_bytes = (size_t)std::max(1, nstage_counter) * 4;
   st->gemv_of_stage.assign(kinds.size(), -1);
   *out = st;
   return NMS_OK;
