@@ -96,6 +96,7 @@ def parse_args():
     p.add_argument("--next-prefetch", type=int, default=0,
                    help="bytes of the following GEMV's weights prefetched into L2 by each launch")
     p.add_argument("--no-dense", action="store_true", help="skip the dense controls")
+    p.add_argument("--no-compile", action="store_true", help="skip the torch.compile dense control")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--cpu-layers", type=int, default=2)
     p.add_argument("--mode", choices=["auto", "persistent", "plan"], default="auto",
@@ -104,6 +105,10 @@ def parse_args():
     p.add_argument("--layers", type=int, default=0,
                    help="profiling only: keep the model's shapes but this many decoder layers")
     p.add_argument("--vocab", type=int, default=0, help="profiling only: override the vocabulary size")
+    p.add_argument("--sub-model", default="qwen3-32b:16:32",
+                   help="second workload timed in the same run at the same N (BASELINE config 5, the "
+                        "tensor-parallel model), as model:n:m; 'none' skips it")
+    p.add_argument("--sub-steps", type=int, default=200)
     return p.parse_args()
 
 
@@ -232,6 +237,62 @@ def time_graph_stats(graph, stream, steps: int, warmup: int, world: int, inner: 
         t = torch.tensor([out["median"], out["mean"], out["stdev"]], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out["median"], out["mean"], out["stdev"] = (float(v) for v in t.tolist())
+    return out
+
+
+def sub_record(args, world: int, rank: int, dev, peaks: dict) -> dict:
+    """ms/token of a second model at the same GPU count (tensor parallel over
+    the ranks for N > 1): BASELINE config 5, Qwen3-32B architecture 16:32 by
+    default, fixed-context CUDA-graph decode at the same CTX, max over ranks;
+    with its weight-bytes roofline per GPU."""
+    from spmv_decode_b200.engine import DecodeEngine
+    from spmv_decode_b200.generate import build_model
+    from spmv_decode_b200.model import ModelArgs
+
+    name, n, m = args.sub_model.split(":")
+    nm = (int(n), int(m))
+    cfg = ModelArgs.from_name(name)
+    max_seq = args.ctx + 8
+    t0 = time.time()
+    if world > 1:
+        from spmv_decode_b200.tp import build_tp_engine
+
+        eng, tp = build_tp_engine(cfg, nm, world, rank, dev, max_seq=max_seq, seed=args.seed, history_len=8,
+                                  mode=args.mode)
+    else:
+        tp = None
+        model = build_model(cfg, nm=nm, device=dev, seed=args.seed, init="device")
+        eng = DecodeEngine(model, max_seq, history_len=8, mode=args.mode)
+    build_s = time.time() - t0
+    eng.fill_synthetic_cache(args.ctx, seed=args.seed)
+    eng.token_in.fill_(123)
+    graph = eng.capture(advance=False)
+    stream = torch.cuda.current_stream(dev)
+    st = time_graph_stats(graph, stream, args.sub_steps, 10, world, args.inner)
+    sb = eng.step_bytes(args.ctx)
+    if world > 1:
+        t = torch.tensor([float(sb["total"])], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        per_gpu = float(t.item())
+    else:
+        per_gpu = float(sb["total"])
+    ideal = per_gpu / peaks["hbm_gbs"] / 1e6
+    out = {"workload": f"{name}-arch {n}:{m} decode, ctx {args.ctx}, batch 1", "parallelism": f"tp{world}",
+           "executor": eng.mode, "ms_per_token": round(st["median"], 4), "mean_ms": round(st["mean"], 4),
+           "steps": st["steps"], "bytes_per_gpu_per_token": int(per_gpu), "ideal_ms": round(ideal, 4),
+           "frac_of_hbm_roofline": round(ideal / st["median"], 4), "build_s": round(build_s, 1),
+           "note": "max over ranks; weight-bytes roofline of the busiest GPU at the measured HBM bandwidth"}
+    pub = PUBLISHED.get((name, f"{n}:{m}"))
+    if pub is not None:
+        out["published_reference"] = {"value": pub[0], "hardware": pub[1], "source": pub[2]}
+    del graph
+    eng.close()
+    if tp is not None:
+        if world > 1:
+            dist.barrier()
+        tp.close()
+    del eng
+    torch.cuda.empty_cache()
     return out
 
 
@@ -456,6 +517,11 @@ def main():
         del model
     torch.cuda.empty_cache()
 
+    # ---- second workload at the same N (the tensor-parallel model) -----------
+    sub = None
+    if args.sub_model != "none" and not args.layers and not args.vocab:
+        sub = sub_record(args, world, rank, dev, peaks)
+
     # ---- dense controls ------------------------------------------------------
     dense = None
     if not args.no_dense and nm is not None and world == 1:
@@ -491,10 +557,37 @@ def main():
             with torch.cuda.graph(g3, stream=s3):
                 torch.argmax(dmodel(None, idx, ipos)[0, -1])
             dense["cublas_graph_ms"] = round(time_graph(g3, stream, max(20, args.steps // 4), 10, world), 4)
-        del g3, dmodel
+            del g3
+            # The reference's dense protocol: torch.compile(decode_one_token,
+            # mode="default"), then CUDA-graph capture of the compiled step
+            # (benchmarks/bench_llama_3_8b_fp16_fixed_ptx.py:155-170).
+            if not args.no_compile:
+                t_c = time.time()
+                try:
+                    step = torch.compile(lambda i, p: torch.argmax(dmodel(None, i, p)[0, -1]), mode="default")
+                    with torch.cuda.stream(s3):
+                        for _ in range(3):
+                            step(idx, ipos)
+                    stream.wait_stream(s3)
+                    torch.cuda.synchronize()
+                    g4 = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g4, stream=s3):
+                        step(idx, ipos)
+                    dense["torch_compile_graph_ms"] = round(
+                        time_graph(g4, stream, max(20, args.steps // 4), 10, world), 4)
+                    del g4
+                except Exception as exc:  # the control is reported, not required
+                    dense["torch_compile_graph_ms"] = None
+                    dense["torch_compile_error"] = f"{type(exc).__name__}: {str(exc)[:200]}"
+                dense["torch_compile_s"] = round(time.time() - t_c, 1)
+        del dmodel
         torch.cuda.empty_cache()
         dense["speedup_vs_engine_dense"] = round(dense["engine_dense_ms"] / ms, 3)
         dense["speedup_vs_cublas"] = round(dense["cublas_graph_ms"] / ms, 3)
+        candidates = {k: dense.get(k) for k in ("engine_dense_ms", "cublas_graph_ms", "torch_compile_graph_ms")}
+        best_k = min((k for k, v in candidates.items() if v), key=lambda k: candidates[k])
+        dense["best_dense"] = best_k
+        dense["speedup_vs_best_dense"] = round(candidates[best_k] / ms, 3)
 
     # ---- CPU baseline (rank 0, N=1) -----------------------------------------
     cpu = None
@@ -530,6 +623,7 @@ def main():
             "gpu_launches": launches_per_step * st["steps"],
             "clocks": clk,
             "dense": dense,
+            "sub": sub,
             "baseline_published": None if pub is None else {"value": pub[0], "hardware": pub[1], "source": pub[2]},
             "build_s": round(build_s, 1),
             "device_error": dev_err,
