@@ -19,6 +19,13 @@ For every shape (out x in) and N:M ratio: seeded synthetic shared-mask weights
                   same shape (the control);
 * ``rowwise``  -- the per-row layout (top-|w| per row and
                   group, one uint8 offset per kept value) at 32:64;
+* ``triton_ref`` (``--triton-ref``) -- the reference's own Triton kernel,
+                  ``nmsparse_spmv_forward_triton_ptx`` (triton_spmv.py:229-318:
+                  fp32 zero-fill, ``nmsparse_generic_kernel`` on this GPU --
+                  the A100 variant is gated to sm80/sm86, :222-226 -- and the
+                  fp16 cast), unmodified, imported from the reference install
+                  in ``baseline/_ref``; a comparison arm only, nothing in the
+                  library imports it;
 
 ``--gemm 16,128,...`` instead times the prefill / batch > 1 GEMM
 (``nmsparse::gemm_packed``: gather + tcgen05 GEMM) against cuBLAS dense
@@ -103,7 +110,24 @@ def _max_rel(y: torch.Tensor, ref: torch.Tensor) -> float:
     return float((y.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
 
 
-def bench_shape(h: int, K: int, ratios, dev, reps: int, peak: float) -> list:
+def _triton_reference():
+    """The reference's Triton GEMV module from ``baseline/_ref`` (None, reason)
+    when it is not installed or does not import."""
+    import sys
+
+    ref_dir = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    if not (ref_dir / "triton_spmv.py").exists():
+        return None, f"reference not installed in {ref_dir}"
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    try:
+        import triton_spmv  # noqa: the reference's module, unmodified
+    except Exception as exc:  # reported, not required
+        return None, f"{type(exc).__name__}: {exc}"[:300]
+    return triton_spmv, None
+
+
+def bench_shape(h: int, K: int, ratios, dev, reps: int, peak: float, triton_ref: bool = False) -> list:
     lib = _lib.lib()
     rows = []
     x = torch.randn(K, device=dev, generator=torch.Generator(device=dev).manual_seed(1)).to(torch.float16)
@@ -182,6 +206,32 @@ def bench_shape(h: int, K: int, ratios, dev, reps: int, peak: float) -> list:
         # every copy shares mask 0 here: the kernel's bytes and access pattern do not depend on the mask
         t_ref = _graph_time_us([ref_fn(i) for i in range(nb)], dev, reps)
         ref_err = _max_rel(outs[0], masked_dense(refm[0], mi0, K, m).float() @ x.float())
+        tri = {}
+        if triton_ref:
+            mod, why = _triton_reference()
+            if mod is None:
+                tri = {"triton_ref_error": why}
+            else:
+                vec = x.view(1, K)
+                ys = [None] * nb
+
+                def tri_fn(i):
+                    def f(s):
+                        ys[i] = mod.nmsparse_spmv_forward_triton_ptx(vec, refm[i], mi0, w, h, n, 128, m, 1, K)
+                    return f
+
+                try:
+                    t_tri = _graph_time_us([tri_fn(i) for i in range(nb)], dev, reps)
+                    tri_fn(0)(None)
+                    torch.cuda.synchronize(dev)
+                    tri = {"triton_ref_us": round(t_tri, 3), "triton_ref_GBs": round(alg / t_tri / 1e3, 1),
+                           "triton_ref_frac": round(alg / t_tri / 1e3 / peak, 3),
+                           "triton_ref_max_rel": _max_rel(ys[0].view(-1), masked_dense(refm[0], mi0, K, m).float()
+                                                          @ x.float()),
+                           "speedup_vs_triton_ref": round(t_tri / t_packed, 3)}
+                except Exception as exc:
+                    tri = {"triton_ref_error": f"{type(exc).__name__}: {exc}"[:300]}
+                del ys
         del refm, outs
         torch.cuda.empty_cache()
         rows.append({
@@ -196,6 +246,7 @@ def bench_shape(h: int, K: int, ratios, dev, reps: int, peak: float) -> list:
             "ref_layout_max_rel": ref_err,
             "cublas_dense_us": round(t_dense, 3), "cublas_dense_GBs": round(dense_bytes / t_dense / 1e3, 1),
             "speedup_vs_cublas": round(t_dense / t_packed, 3),
+            **tri,
         })
         print(json.dumps(rows[-1]), flush=True)
     return rows
@@ -320,6 +371,9 @@ def main(argv=None):
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--no-head", action="store_true")
     p.add_argument("--no-rowwise", action="store_true")
+    p.add_argument("--triton-ref", action="store_true",
+                   help="also time the reference's Triton kernel from baseline/_ref (a comparison arm)")
+    p.add_argument("--out", default="", help="also write the rows as JSON to this file")
     p.add_argument("--gemm", default="", help="token counts for the prefill GEMM, e.g. 16,128,512,2048 "
                                               "(runs only the GEMM table)")
     args = p.parse_args(argv)
@@ -337,13 +391,15 @@ def main(argv=None):
                           "rows": len(rows)}), flush=True)
         return rows
     for h, K in shapes:
-        rows += bench_shape(h, K, ratios, dev, args.reps, peak)
+        rows += bench_shape(h, K, ratios, dev, args.reps, peak, triton_ref=args.triton_ref)
     if not args.no_rowwise:
         for h, K in shapes:
             rows.append(bench_rowwise(h, K, 32, 64, dev, args.reps, peak))
     if not args.no_head:
         rows.append(bench_dense_head(dev, args.reps, peak))
     print(json.dumps({"summary": True, "peak_GBs": peak, "peak_source": src, "rows": len(rows)}), flush=True)
+    if args.out:
+        Path(args.out).write_text(json.dumps({"peak_GBs": peak, "peak_source": src, "rows": rows}, indent=1))
     return rows
 
 
