@@ -221,6 +221,15 @@ __device__ __forceinline__ float ld_dsmem_f32(const float* local_ptr, uint32_t r
   return v;
 }
 
+// Atomic add with acquire-release semantics at GPU scope (one round trip):
+// publishes the writes this thread has observed (including the CTA's, after
+// a block barrier) and returns the previous value with acquire ordering.
+__device__ __forceinline__ unsigned atom_add_acq_rel_u32(unsigned* p, unsigned v) {
+  unsigned prev;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(prev) : "l"(p), "r"(v) : "memory");
+  return prev;
+}
+
 // ---------------------------------------------------------------------------
 // Small reductions.
 // ---------------------------------------------------------------------------

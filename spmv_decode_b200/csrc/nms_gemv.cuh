@@ -214,15 +214,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
       }
       p.amax_val[cta] = bv;
       p.amax_idx[cta] = bi;
-      __threadfence();
-      const uint32_t prev = atomicAdd(p.amax_counter, 1u);
+      const uint32_t prev = atom_add_acq_rel_u32(p.amax_counter, 1u);
       s_last = (prev == ncta - 1) ? 1 : 0;
     }
     __syncthreads();
     if (s_last) {
-      // Last CTA to finish: reduce all partials (written before each CTA's
-      // fence + counter increment, so they are visible here).
-      __threadfence();
+      // Last CTA to finish: reduce all partials (each CTA wrote its partial
+      // before its acquire-release counter add, so they are visible here).
       float fv = -INFINITY;
       int fi = 0x7fffffff;
       for (int q = tid; q < (int)ncta; q += NT) {

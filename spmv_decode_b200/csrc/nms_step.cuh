@@ -144,8 +144,7 @@ __device__ __forceinline__ void step_exit(unsigned* count, unsigned* exit_count,
                                           unsigned long long* epoch) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(exit_count, 1u);
+    const unsigned prev = atom_add_acq_rel_u32(exit_count, 1u);
     if (prev == ncta - 1) {
       atomicExch(count, 0u);
       atomicExch(exit_count, 0u);
@@ -847,13 +846,13 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, 
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(&head_count[kvh], 1u);
+    // One acquire-release add: it publishes this CTA's partial state (the
+    // block barrier above makes the other threads' stores part of it) and,
+    // for the last unit of the head, makes every other unit's state visible
+    // -- cheaper than a sequentially consistent fence on each side.
+    const unsigned prev = atom_add_acq_rel_u32(&head_count[kvh], 1u);
     S.last = (prev == (unsigned)p.splits - 1) ? 1 : 0;
-    if (S.last) {
-      __threadfence();
-      head_count[kvh] = 0u;
-    }
+    if (S.last) head_count[kvh] = 0u;
   }
   __syncthreads();
   trace_at(td, 5);
