@@ -261,3 +261,41 @@ def test_abort_request_voids_step_and_engine_recovers(cuda_device):
         assert tok == ref_tok
         assert torch.equal(logits, ref_logits)
     eng.close()
+
+
+@pytest.mark.parametrize("kind", ["llama", "qwen3"])
+def test_flow_step_reference_fixture(cuda_device, kind):
+    """The opt-in dataflow step (nms_step_create_flow) on the reference's own
+    decode fixtures: same tokens, logits within the decode bar."""
+    z = np.load(GOLDEN / f"decode_{kind}_tiny.npz")
+    model, prompt_len, steps = _model_from_golden(z, kind, cuda_device)
+    eng = DecodeEngine(model, 64, history_len=64, mode="flow")
+    assert eng.mode == "flow"
+    toks, logits = GraphDecoder(eng).run(z["prompt"].tolist(), steps + 1, keep_logits=True)
+    ref = _f16(z["logits"]).float()
+    err = (logits.float().cpu() - ref).abs().amax(dim=1)
+    assert bool((err <= LOGIT_TOL * ref.abs().amax(dim=1)).all())
+    assert toks == z["tokens"].tolist()
+    assert _lib.device_error() == 0
+    eng.close()
+
+
+@pytest.mark.parametrize("name, nm", [("llama-3.1-8b", (32, 64)), ("qwen3-32b", (16, 32))])
+def test_flow_step_matches_barrier_step(cuda_device, name, nm):
+    """Dataflow and barrier kernels on the same 2-layer model at full widths:
+    the greedy tokens agree and the logits stay within 2e-3 relative (the
+    norm statistic is summed in a different order)."""
+    args = ModelArgs.from_name(name)
+    args.n_layer = 2
+    model = build_model(args, nm=nm, device=cuda_device, seed=21, init="device")
+    out = {}
+    for mode in ("barrier", "flow"):
+        eng = DecodeEngine(model, 64, history_len=64, mode=mode)
+        assert eng.mode == ("flow" if mode == "flow" else "persistent")
+        out[mode] = GraphDecoder(eng).run([3, 17, 29], 12, keep_logits=True)
+        assert _lib.device_error() == 0
+        eng.close()
+    (tb, lb), (tf, lf) = out["barrier"], out["flow"]
+    rel = ((lf.float() - lb.float()).abs().amax(dim=1) / lb.float().abs().amax(dim=1)).max().item()
+    assert rel <= 2e-3, rel
+    assert tf == tb
