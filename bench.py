@@ -97,6 +97,7 @@ def parse_args():
                    help="bytes of the following GEMV's weights prefetched into L2 by each launch")
     p.add_argument("--no-dense", action="store_true", help="skip the dense controls")
     p.add_argument("--no-compile", action="store_true", help="skip the torch.compile dense control")
+    p.add_argument("--no-sampled", action="store_true", help="skip the temperature-1.0 sampled-step timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--cpu-layers", type=int, default=2)
     p.add_argument("--mode", choices=["auto", "persistent", "plan"], default="auto",
@@ -468,6 +469,22 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    # ---- the reference's timed work includes sampling: the same step with ----
+    # ---- temperature 1.0 (generate.py:46-63, top_k None as in its bench) ----
+    sampled = None
+    if world == 1 and not args.no_sampled:
+        seng = DecodeEngine(model, max_seq, history_len=8, mode=args.mode, temperature=1.0, sample_seed=args.seed)
+        seng.fill_synthetic_cache(args.ctx, seed=args.seed)
+        seng.token_in.fill_(123)
+        sg_ = seng.capture(advance=False)
+        sst = time_graph_stats(sg_, stream, max(20, args.steps // 4), 10, world, args.inner)
+        sampled = {"temperature": 1.0, "top_k": None, "ms_per_token": round(sst["median"], 4),
+                   "note": "same step, token sampled from softmax(logits) in the head kernel (Gumbel-max with "
+                           "Philox4x32-10 noise), as the reference's timed decode samples"}
+        del sg_
+        seng.close()
+        del seng
+
     # ---- roofline: the sparse GEMV kernel timed live --------------------------
     plan, gemv_bytes = eng.gemv_plan()
     n_gemv = sum(1 for r in eng.gemv_records if not r["argmax"])
@@ -624,6 +641,7 @@ def main():
             "clocks": clk,
             "dense": dense,
             "sub": sub,
+            "sampled": sampled,
             "baseline_published": None if pub is None else {"value": pub[0], "hardware": pub[1], "source": pub[2]},
             "build_s": round(build_s, 1),
             "device_error": dev_err,

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NMS_ABI_VERSION 1
+#define NMS_ABI_VERSION 2
 
 enum nms_status {
   NMS_OK = 0,
@@ -203,6 +203,17 @@ typedef struct nms_gemv_fused_args {
    * (model.py:164) folded into the first GEMV of a decode step. */
   const int64_t* x_token;
   int64_t x_rows;
+  /* Temperature sampling (NMS_EPI_ARGMAX only; temperature 0 = greedy): the
+   * token is argmax(logit / temperature + g), g Gumbel(0, 1) noise from
+   * Philox4x32-10 keyed by sample_seed and counted by (vocabulary row +
+   * sample_row_offset, *sample_pos) -- a sample of softmax(logit /
+   * temperature), the reference's sample() without top_k
+   * (generate.py:46-63: argmax(probs / q), q ~ Exp(1)).  sample_pos may be
+   * NULL (position 0). */
+  float temperature;
+  uint64_t sample_seed;
+  const int64_t* sample_pos;
+  int64_t sample_row_offset;
 } nms_gemv_fused_args;
 
 int nms_gemv_fused_f16(const nms_gemv_fused_args* args, void* stream);

@@ -22,6 +22,7 @@ NMS_ERR_NOT_IMPLEMENTED = -3
 NMS_ERR_CUDA = -4
 NMS_ERR_DEVICE = -5
 
+ABI_VERSION = 2  # NMS_ABI_VERSION of include/nmsparse_b200.h these declarations match
 NMS_MAX_SEGMENTS = 4
 NMS_EPI_STORE = 0
 NMS_EPI_SWIGLU = 1
@@ -132,6 +133,10 @@ class NmsGemvFusedArgs(ctypes.Structure):
         ("next_prefetch_head", c_i64),
         ("x_token", c_void_p),
         ("x_rows", c_i64),
+        ("temperature", ctypes.c_float),
+        ("sample_seed", ctypes.c_uint64),
+        ("sample_pos", c_void_p),
+        ("sample_row_offset", c_i64),
     ]
 
 
@@ -223,8 +228,12 @@ def lib() -> ctypes.CDLL:
                 "(there is no CPU or Triton fallback)"
             )
         mode = os.RTLD_NOW | getattr(os, "RTLD_GLOBAL", 0)
-        _LIB = ctypes.CDLL(str(LIB_PATH), mode=mode)
-        _declare(_LIB)
+        handle = ctypes.CDLL(str(LIB_PATH), mode=mode)
+        _declare(handle)
+        if handle.nms_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"{LIB_PATH} has ABI {handle.nms_abi_version()}, these bindings expect {ABI_VERSION}; "
+                               "rebuild it with `python -m spmv_decode_b200.build`")
+        _LIB = handle
     return _LIB
 
 

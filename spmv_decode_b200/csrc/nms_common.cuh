@@ -231,6 +231,42 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_u32(unsigned* p, unsigned v
 }
 
 // ---------------------------------------------------------------------------
+// Counter-based random numbers for temperature sampling: Philox4x32-10
+// (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3",
+// SC 2011), ten rounds of two 32x32->64 multiplies with the round keys bumped
+// by the Weyl constants.  Stateless: the same (key, counter) gives the same
+// four words on any CTA, GPU or host restatement.
+// ---------------------------------------------------------------------------
+__host__ __device__ inline void philox4x32_10(uint32_t (&c)[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) {
+      k0 += 0x9E3779B9u;
+      k1 += 0xBB67AE85u;
+    }
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = (uint32_t)p1;
+    c[2] = n2;
+    c[3] = (uint32_t)p0;
+  }
+}
+
+// Gumbel(0, 1) noise for vocabulary row `row` at token position `pos`:
+// -log(-log(u)), u uniform in (0, 1) from the top 24 bits of the first
+// Philox word.  argmax(logit / T + noise) is a sample of softmax(logit / T)
+// -- the reference's exponential race argmax(probs / q), q ~ Exp(1)
+// (generate.py:46-48), written with log(q) = log(-log(u)).
+__device__ __forceinline__ float gumbel_noise(uint64_t seed, int64_t pos, int64_t row) {
+  uint32_t c[4] = {(uint32_t)row, (uint32_t)pos, (uint32_t)((uint64_t)pos >> 32), 0x5EED5A3Bu};
+  philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+  const float u = ((float)(c[0] >> 8) + 0.5f) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
+}
+
+// ---------------------------------------------------------------------------
 // Small reductions.
 // ---------------------------------------------------------------------------
 template <int L>

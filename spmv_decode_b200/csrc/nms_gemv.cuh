@@ -81,6 +81,14 @@ struct GemvParams {
   int64_t* token_history;  // history[*pos] = token
   int64_t* pos;            // position counter, incremented after the above
   int64_t history_len;     // entries in token_history
+  // Temperature sampling in the argmax epilogue (temperature > 0): the token
+  // is argmax(logit / temperature + Gumbel noise(seed, *sample_pos, row +
+  // sample_row_offset)) -- a sample of softmax(logit / temperature).
+  float temperature;       // 0: greedy argmax
+  int32_t pad_s;
+  uint64_t sample_seed;
+  const int64_t* sample_pos;  // noise counter (the token position), or nullptr (0)
+  int64_t sample_row_offset;  // global vocabulary row of local row 0 (vocabulary-parallel head)
 };
 
 // Position of compressed element j inside the permuted shared-memory copy of
@@ -178,11 +186,16 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
   } else {  // argmax
     float bv = -INFINITY;
     int bi = 0x7fffffff;
+    const bool sample = p.temperature > 0.f;
+    const float inv_t = sample ? 1.0f / p.temperature : 1.f;
+    const int64_t spos = (sample && p.sample_pos != nullptr) ? *p.sample_pos : 0;
     for (int v = tid; v < nrows; v += NT) {
       const __half hv = f2h(s_acc[v]);
       p.out[row_lo + v] = hv;
-      const float fv = h2f(hv);
       const int row = row_lo + v;
+      // The fp16 logit (greedy), or its sampling key.
+      const float fv = sample ? h2f(hv) * inv_t + gumbel_noise(p.sample_seed, spos, row + p.sample_row_offset)
+                              : h2f(hv);
       if (fv > bv || (fv == bv && row < bi)) {
         bv = fv;
         bi = row;

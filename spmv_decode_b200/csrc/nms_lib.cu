@@ -373,6 +373,14 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
   p.history_len = a->history_len;
   if (epi != nms::kEpiArgmax && (a->next_token || a->token_history || a->pos))
     return fail(NMS_ERR_VALUE, "generation hooks need the argmax epilogue");
+  if (!(a->temperature >= 0.f) || a->temperature > 1e30f)
+    return fail(NMS_ERR_VALUE, "temperature must be finite and >= 0 (got %g)", (double)a->temperature);
+  if (a->temperature > 0.f && epi != nms::kEpiArgmax)
+    return fail(NMS_ERR_VALUE, "temperature sampling needs the argmax epilogue");
+  p.temperature = a->temperature;
+  p.sample_seed = a->sample_seed;
+  p.sample_pos = a->sample_pos;
+  p.sample_row_offset = a->sample_row_offset;
 
   int grid = a->grid > 0 ? a->grid : dev->num_sms * kGemvCtasPerSm;
   if (grid > p.row_groups) grid = p.row_groups;

@@ -928,9 +928,15 @@ __device__ __forceinline__ void attention_unit(const AttnParams& p, int pos_in, 
 // the rank's (logit, global index) candidate goes to point `nreduce` of every
 // rank's area; the largest logit wins, the lowest index on ties -- the token
 // argmax over the full logits gives.  Then the head's generation hooks.
-__device__ __forceinline__ void tp_head_token(const StepParams& sp, const __half* logits, unsigned long long epoch) {
+__device__ __forceinline__ void tp_head_token(const StepParams& sp, const GemvParams& hp, unsigned long long epoch) {
+  const __half* logits = hp.out;
   const int64_t li = *reinterpret_cast<volatile int64_t*>(sp.tp_local_best);
-  const float lv = h2f(logits[li]);
+  // The rank's candidate value: its winner's fp16 logit, or (temperature
+  // sampling) the same key the local argmax compared.
+  float lv = h2f(logits[li]);
+  if (hp.temperature > 0.f)
+    lv = lv * (1.0f / hp.temperature) +
+         gumbel_noise(hp.sample_seed, hp.sample_pos != nullptr ? *hp.sample_pos : 0, li + hp.sample_row_offset);
   const uint32_t tag = tp_tag(sp, epoch, sp.tp_nreduce);
   const size_t slot = ((size_t)sp.tp_nreduce * sp.tp_world + sp.tp_rank) * sp.tp_dim;
   for (int r = 0; r < sp.tp_world; ++r) {
@@ -1152,7 +1158,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     // logits: one grid barrier, then CTA 0 swaps candidates with the peers.
     grid_arrive(sp.bar_count);
     if (grid_wait(sp.bar_count, ncta, (unsigned)sp.nstages - 1u) && cta == 0 && tid == 0)
-      tp_head_token(sp, s_g[(gn - 1) & 1].g.out, epoch);
+      tp_head_token(sp, s_g[(gn - 1) & 1].g, epoch);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   step_exit(sp.bar_count, sp.bar_exit, ncta, sp.tp_world > 1 ? sp.tp_epoch : nullptr);

@@ -77,7 +77,8 @@ class DecodeEngine:
     def __init__(self, model: Transformer, max_seq_length: int, *, pdl: bool = True, prefetch_bytes: int = 0,
                  next_prefetch_bytes: int = 0, attn_splits: int = 0, history_len: int = 0, mode: str = "auto",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None, tp_rank: int = 0, tp_size: int = 1,
-                 local_heads: Optional[tuple] = None, head_hook: Optional[Callable[[bool], None]] = None):
+                 local_heads: Optional[tuple] = None, head_hook: Optional[Callable[[bool], None]] = None,
+                 temperature: float = 0.0, sample_seed: int = 0, vocab_offset: int = 0):
         c = model.config
         self.config = c
         self.model = model
@@ -95,6 +96,14 @@ class DecodeEngine:
         if mode not in ("auto", "persistent", "flow", "barrier", "plan"):
             raise ValueError(f"unknown mode {mode!r}")
         self.tp_rank, self.tp_size = tp_rank, tp_size
+        # Head: greedy argmax (temperature 0) or a sample of softmax(logits /
+        # temperature) -- the reference's sample() without top_k
+        # (generate.py:46-63), drawn with counter-based noise keyed by
+        # sample_seed and the token position.
+        if not (temperature >= 0.0 and math.isfinite(temperature)):
+            raise ValueError(f"temperature must be finite and >= 0, got {temperature}")
+        self.temperature, self.sample_seed = float(temperature), int(sample_seed)
+        self.vocab_offset = int(vocab_offset)
         Hq, Hkv = local_heads if local_heads is not None else (c.n_head, c.n_local_heads)
         self.Hq, self.Hkv, self.D = Hq, Hkv, c.head_dim
         self.max_seq_length = int(max_seq_length)
@@ -214,6 +223,10 @@ class DecodeEngine:
             a.amax_counter = self.amax_counter.data_ptr()
             a.token_out = self.token_out.data_ptr()
             a.amax_capacity = ARGMAX_CAPACITY
+            a.temperature = self.temperature
+            a.sample_seed = self.sample_seed & 0xFFFFFFFFFFFFFFFF
+            a.sample_pos = self.pos.data_ptr()
+            a.sample_row_offset = self.vocab_offset
             if advance:
                 a.next_token = self.token_in.data_ptr()
                 a.pos = self.pos.data_ptr()

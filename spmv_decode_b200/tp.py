@@ -261,12 +261,18 @@ class TensorParallel:
 
 def build_tp_engine(cfg, nm: Optional[Tuple[int, int]], world: int, rank: int, device: torch.device, *,
                     max_seq: int, seed: int = 0, prefetch_bytes: int = 0, next_prefetch_bytes: int = 0,
-                    history_len: int = 0, group=None, mode: str = "auto"):
+                    history_len: int = 0, group=None, mode: str = "auto", temperature: float = 0.0,
+                    sample_seed: int = 0):
     """This rank's decode engine for ``cfg`` (the same weights as the
     single-GPU model built with ``seed``), and its TensorParallel state.
     ``mode``: "plan" (NCCL all-reduces between launches), "persistent"
     (all-reduces inside the persistent step over NVLink) or "auto"
-    (persistent when it fits)."""
+    (persistent when it fits).  ``temperature`` > 0 samples the token (the
+    same draw as one GPU: the noise is keyed by the global vocabulary row);
+    it needs the persistent executor, whose exchange compares the sampling
+    keys."""
+    if temperature > 0 and mode == "plan":
+        raise NotImplementedError("temperature sampling under tensor parallelism needs the persistent executor")
     from .engine import DecodeEngine
     from .generate import build_model
 
@@ -276,11 +282,12 @@ def build_tp_engine(cfg, nm: Optional[Tuple[int, int]], world: int, rank: int, d
     tp = TensorParallel(info, device, group)
     eng = DecodeEngine(model, max_seq, prefetch_bytes=prefetch_bytes, next_prefetch_bytes=next_prefetch_bytes,
                        history_len=history_len, mode="plan", allreduce=tp.allreduce, tp_rank=rank, tp_size=world,
-                       local_heads=info.local_heads, head_hook=lambda adv: tp.head_hook(eng, adv))
+                       local_heads=info.local_heads, head_hook=lambda adv: tp.head_hook(eng, adv),
+                       temperature=temperature, sample_seed=sample_seed, vocab_offset=info.vocab_offset)
     if mode in ("auto", "persistent"):
         try:
             tp.enable_persistent(eng)
         except NotImplementedError:
-            if mode == "persistent":
+            if mode == "persistent" or temperature > 0:
                 raise
     return eng, tp

@@ -27,7 +27,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert sorted(_lib.EXPORTED_SYMBOLS) == declared
     for name in declared:
         assert hasattr(L, name), name
-    assert L.nms_abi_version() == 1
+    assert L.nms_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_status_names():

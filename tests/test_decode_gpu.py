@@ -299,3 +299,35 @@ def test_flow_step_matches_barrier_step(cuda_device, name, nm):
     rel = ((lf.float() - lb.float()).abs().amax(dim=1) / lb.float().abs().amax(dim=1)).max().item()
     assert rel <= 2e-3, rel
     assert tf == tb
+
+
+@pytest.mark.parametrize("mode", ["persistent", "plan"])
+def test_temperature_sampling_matches_oracle(cuda_device, mode):
+    """Temperature sampling in the head (the reference's sample() at
+    temperature T without top_k, generate.py:46-63): every token equals the
+    oracle's Gumbel-max draw -- Philox4x32-10 noise keyed by the seed and the
+    token position -- over the engine's own fp16 logits, except where two
+    keys are within 1e-4 (logf rounding); the same seed draws the same
+    tokens again, another seed draws others."""
+    from oracle.sample_oracle import sample_keys
+
+    model = build_model(ModelArgs(block_size=64, vocab_size=1024, n_layer=2, n_head=4, n_local_heads=2, dim=512,
+                                  intermediate_size=1024), nm=(8, 16), device=cuda_device, seed=31)
+    T, seed = 0.7, 0x5EED
+    runs = []
+    for s in (seed, seed, seed + 1):
+        eng = DecodeEngine(model, 64, history_len=64, mode=mode, temperature=T, sample_seed=s)
+        toks, logits = GraphDecoder(eng).run([5, 9], 24, keep_logits=True)
+        assert _lib.device_error() == 0
+        eng.close()
+        runs.append(toks)
+        if s != seed or len(runs) > 1:
+            continue
+        lg = logits.cpu().numpy()
+        for i, tok in enumerate(toks):
+            pos = 1 + i  # the step at position 1 + i drew token i
+            keys = sample_keys(lg[pos], T, pos, seed)
+            best = int(np.argmax(keys))
+            assert tok == best or keys[best] - keys[tok] < 1e-4, (i, tok, best)
+    assert runs[0] == runs[1]
+    assert runs[0] != runs[2]

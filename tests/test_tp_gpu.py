@@ -41,7 +41,7 @@ def _cfg(name="toy"):
 NM = {"toy": (16, 32), "llama": (32, 64), "qwen32": (16, 32)}
 
 
-def _rank(rank, world, port, out, mode, name="toy"):
+def _rank(rank, world, port, out, mode, name="toy", temperature=0.0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     from datetime import timedelta
 
@@ -53,7 +53,7 @@ def _rank(rank, world, port, out, mode, name="toy"):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
     try:
         eng, tp = build_tp_engine(_cfg(name), NM[name], world, rank, dev, max_seq=64, seed=5, history_len=64,
-                                  mode=mode)
+                                  mode=mode, temperature=temperature, sample_seed=77)
         assert eng.mode == ("persistent_tp" if mode == "persistent" else "plan"), eng.mode
         gd = GraphDecoder(eng)
         toks, logits = gd.run(PROMPT, STEPS, keep_logits=True)
@@ -124,3 +124,33 @@ def test_tp_engine_matches_single_gpu(world, name, mode):
         assert (row[b] - row[a]).item() <= 2 * err[first + diverge].item(), (diverge, a, b)
     print(f"tp{world} {name} {mode}: worst rel logit err {(err / scale).max().item():.2e}, "
           f"tokens {'identical' if diverge is None else f'near-tie at step {diverge}'}")
+
+
+def test_tp2_temperature_sampling_matches_single_gpu():
+    """Sampling under tensor parallelism draws the single-GPU engine's tokens:
+    the noise is keyed by the global vocabulary row, and the ranks exchange
+    sampling keys instead of logits."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from spmv_decode_b200.engine import DecodeEngine
+    from spmv_decode_b200.generate import GraphDecoder, build_model
+
+    dev = torch.device("cuda:0")
+    model = build_model(_cfg("toy"), nm=NM["toy"], device=dev, seed=5, init="device")
+    eng = DecodeEngine(model, 64, history_len=64, temperature=1.0, sample_seed=77)
+    ref_toks, _ = GraphDecoder(eng).run(PROMPT, STEPS, keep_logits=True)
+    eng.close()
+    del eng, model
+    torch.cuda.empty_cache()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + (os.getpid() % 1000)
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, "persistent", "toy", 1.0)) for r in range(2)]
+    for p in procs:
+        p.start()
+    toks, _, dev_err = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert dev_err == 0
+    assert toks == ref_toks
