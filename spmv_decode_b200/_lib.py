@@ -31,6 +31,7 @@ NMS_PRO_PLAIN = 0
 NMS_PRO_RESID_RMSNORM = 1
 NMS_FLAG_PDL = 1
 NMS_FLAG_DENSE = 2
+NMS_FLAG_REGISTER_RING = 4
 NMS_ROPE_INTERLEAVED = 0
 NMS_ROPE_HALF = 1
 NMS_DTYPE_F16 = 0

@@ -34,6 +34,7 @@
 #include "nms_gemv.cuh"
 #include "nms_step.cuh"
 #include "nms_flow.cuh"
+#include "nms_gemv_ring.cuh"
 
 namespace {
 
@@ -92,6 +93,12 @@ int device_info(const DeviceInfo** out) {
         (const void*)nms::gemv_packed_kernel<32>, (const void*)nms::gemv_packed_kernel<16>,
         (const void*)nms::gemv_packed_kernel<8>,  (const void*)nms::gemv_packed_kernel<4>,
         (const void*)nms::gemv_ref_kernel<8, false>, (const void*)nms::gemv_ref_kernel<8, true>,
+        (const void*)nms::gemv_ring_kernel<32, 8>, (const void*)nms::gemv_ring_kernel<16, 8>,
+        (const void*)nms::gemv_ring_kernel<8, 8>,  (const void*)nms::gemv_ring_kernel<4, 8>,
+        (const void*)nms::gemv_ring_kernel<32, 6>, (const void*)nms::gemv_ring_kernel<16, 6>,
+        (const void*)nms::gemv_ring_kernel<8, 6>,  (const void*)nms::gemv_ring_kernel<4, 6>,
+        (const void*)nms::gemv_ring_kernel<32, 4>, (const void*)nms::gemv_ring_kernel<16, 4>,
+        (const void*)nms::gemv_ring_kernel<8, 4>,  (const void*)nms::gemv_ring_kernel<4, 4>,
     };
     size_t static_max = 0;
     for (const void* k : dyn_smem_kernels) {
@@ -101,6 +108,18 @@ int device_info(const DeviceInfo** out) {
       if (fa.sharedSizeBytes > static_max) static_max = fa.sharedSizeBytes;
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem - (int)fa.sharedSizeBytes);
       if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+    }
+    // The ring GEMV keeps its CTA at most half an SM so that the next
+    // launch's CTA fits beside it: ask for the largest shared-memory carveout
+    // (the default sizes the carveout for one CTA's need).
+    for (const void* k : {(const void*)nms::gemv_ring_kernel<32, 8>, (const void*)nms::gemv_ring_kernel<16, 8>,
+                          (const void*)nms::gemv_ring_kernel<8, 8>, (const void*)nms::gemv_ring_kernel<4, 8>,
+                          (const void*)nms::gemv_ring_kernel<32, 6>, (const void*)nms::gemv_ring_kernel<16, 6>,
+                          (const void*)nms::gemv_ring_kernel<8, 6>, (const void*)nms::gemv_ring_kernel<4, 6>,
+                          (const void*)nms::gemv_ring_kernel<32, 4>, (const void*)nms::gemv_ring_kernel<16, 4>,
+                          (const void*)nms::gemv_ring_kernel<8, 4>, (const void*)nms::gemv_ring_kernel<4, 4>}) {
+      e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(PreferredSharedMemoryCarveout)");
     }
     // Dynamic shared memory available to every kernel that takes it.
     d.max_smem_optin = (size_t)smem - static_max;
@@ -184,6 +203,7 @@ struct EmbedParams {
 struct LaunchRec {
   enum Kind { kGemvPacked, kGemvRef, kAttention, kEmbedding, kPack, kUnpack } kind;
   int lanes = 0;  // gemv_packed_kernel template argument
+  int ring_depth = 0;  // > 0: gemv_ring_kernel with this ring depth (lanes as above)
   bool rowwise = false;  // kGemvRef: per-row mask (mat_index [w, h])
   int amax_capacity = 0;  // argmax epilogue: partials the caller's scratch holds
   nms::GemvParams gp;
@@ -200,10 +220,29 @@ struct LaunchRec {
   bool pdl = false;
 };
 
+template <int D>
+cudaError_t launch_gemv_ring_d(const LaunchRec& r, cudaStream_t st) {
+  switch (r.lanes) {
+    case 32: return launch_ex(nms::gemv_ring_kernel<32, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+    case 16: return launch_ex(nms::gemv_ring_kernel<16, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+    case 8: return launch_ex(nms::gemv_ring_kernel<8, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+    default: return launch_ex(nms::gemv_ring_kernel<4, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+  }
+}
+
+cudaError_t launch_gemv_ring(const LaunchRec& r, cudaStream_t st) {
+  return r.ring_depth >= 8 ? launch_gemv_ring_d<8>(r, st)
+                           : (r.ring_depth >= 6 ? launch_gemv_ring_d<6>(r, st) : launch_gemv_ring_d<4>(r, st));
+}
+
 int launch_rec(const LaunchRec& r, cudaStream_t st) {
   cudaError_t e = cudaSuccess;
   switch (r.kind) {
     case LaunchRec::kGemvPacked:
+      if (r.ring_depth > 0) {
+        e = launch_gemv_ring(r, st);
+        break;
+      }
       switch (r.lanes) {
         case 32: e = launch_ex(nms::gemv_packed_kernel<32>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp); break;
         case 16: e = launch_ex(nms::gemv_packed_kernel<16>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp); break;
@@ -395,6 +434,35 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
                 (long long)K, (long long)w_pad, nsegx, smem, dev->max_smem_optin);
   rec->kind = LaunchRec::kGemvPacked;
   rec->lanes = L;
+  rec->ring_depth = 0;
+  if ((a->flags & NMS_FLAG_REGISTER_RING) == 0 && pro == nms::kProPlain && p.pf_items == 0) {
+    // One CTA per SM, so that the next launch's CTA fits beside it; two when
+    // the stream is long (over 256 KB of weights per SM), where more bytes in
+    // flight pay more than the overlap with the neighbouring launches.
+    int64_t wbytes = 0;
+    for (int i = 0; i < a->nseg; ++i) wbytes += a->seg[i].rows * w_pad * 2;
+    int rgrid = a->grid > 0 ? a->grid
+                            : dev->num_sms * (wbytes > (int64_t)dev->num_sms * nms::kRingTwoPerSmBytes ? 2 : 1);
+    if (rgrid > p.row_groups) rgrid = p.row_groups;
+    if (rgrid < 1) rgrid = 1;
+    const int rvrows = (paired ? 2 : 1) * ((p.row_groups + rgrid - 1) / rgrid) * RG;
+    for (int D : {8, 6, 4}) {
+      const size_t rs = nms::gemv_ring_smem_bytes(D, (int)K, (int)w, (int)w_pad, nsegx, rvrows);
+      if (rs <= nms::kRingSmemCap && rs <= dev->max_smem_optin &&
+          !(epi == nms::kEpiArgmax && rgrid > a->amax_capacity)) {
+        rec->ring_depth = D;
+        rec->grid = dim3(rgrid);
+        rec->block = dim3(nms::kRingThreads);
+        rec->smem = rs;
+        break;
+      }
+    }
+  }
+  if (rec->ring_depth > 0) {
+    rec->amax_capacity = (epi == nms::kEpiArgmax) ? a->amax_capacity : 0;
+    rec->pdl = (a->flags & NMS_FLAG_PDL) != 0;
+    return NMS_OK;
+  }
   rec->amax_capacity = (epi == nms::kEpiArgmax) ? a->amax_capacity : 0;
   rec->grid = dim3(grid);
   rec->block = dim3(nms::kGemvThreads);

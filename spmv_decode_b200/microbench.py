@@ -7,10 +7,13 @@ For every shape (out x in) and N:M ratio: seeded synthetic shared-mask weights
 (N(0, 0.02) values, uniform random in-group masks, drawn on the GPU), a vector
 ~N(0, 1); the time of one launch of
 
-* ``packed``   -- ``gemv_packed_kernel`` on the re-laid-out packed weights
-                  (the kernel behind ``nmsparse::gemv_packed`` / NmSparseLinear);
+* ``packed``   -- ``nms_gemv_packed_f16`` on the re-laid-out packed weights
+                  (the kernel behind ``nmsparse::gemv_packed`` / NmSparseLinear:
+                  ``gemv_ring_kernel``, per-warp shared-memory weight rings);
                   ``packed_pdl``: the same launches with programmatic
                   dependent launch, as the decode plan issues them;
+                  ``regring_pdl``: ``gemv_packed_kernel`` (register-ring
+                  streaming, ``NMS_FLAG_REGISTER_RING``) with PDL;
 * ``step``     -- the same GEMV as a one-stage launch of the persistent
                   decode-step kernel (per-warp shared-memory weight rings);
 * ``ref``      -- ``gemv_ref_kernel`` on the reference ``[w, h]`` layout
@@ -170,6 +173,15 @@ def bench_shape(h: int, K: int, ratios, dev, reps: int, peak: float, triton_ref:
             fargs.append(a)
         t_pdl = _graph_time_us([(lambda a: lambda s: _lib.check(lib.nms_gemv_fused_f16(ctypes.byref(a), s.cuda_stream)))(a)
                                 for a in fargs], dev, reps)
+        for a in fargs:
+            a.flags = _lib.NMS_FLAG_PDL | _lib.NMS_FLAG_REGISTER_RING
+        outs[0].zero_()
+        t_reg = _graph_time_us([(lambda a: lambda s: _lib.check(lib.nms_gemv_fused_f16(ctypes.byref(a), s.cuda_stream)))(a)
+                                for a in fargs], dev, reps)
+        p0_, mi0_, _, _ = mats[0]
+        reg_err = _max_rel(outs[0], masked_dense(unpack(p0_, w), mi0_, K, m).float() @ x.float())
+        for a in fargs:
+            a.flags = _lib.NMS_FLAG_PDL
         p0, mi0, _, _ = mats[0]
         ref = masked_dense(unpack(p0, w), mi0, K, m).float() @ x.float()
         packed_err = _max_rel(outs[0], ref)
@@ -240,6 +252,8 @@ def bench_shape(h: int, K: int, ratios, dev, reps: int, peak: float, triton_ref:
             "packed_frac": round(alg / t_packed / 1e3 / peak, 3), "packed_max_rel": packed_err,
             "packed_pdl_us": round(t_pdl, 3), "packed_pdl_GBs": round(alg / t_pdl / 1e3, 1),
             "packed_pdl_frac": round(alg / t_pdl / 1e3 / peak, 3),
+            "regring_pdl_us": round(t_reg, 3), "regring_pdl_frac": round(alg / t_reg / 1e3 / peak, 3),
+            "regring_max_rel": reg_err,
             "step_us": round(t_step, 3), "step_GBs": round(alg / t_step / 1e3, 1),
             "step_frac": round(alg / t_step / 1e3 / peak, 3), "step_max_rel": step_err,
             "ref_layout_us": round(t_ref, 3), "ref_layout_GBs": round(alg / t_ref / 1e3, 1),

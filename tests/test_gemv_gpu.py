@@ -23,6 +23,9 @@ pytestmark = pytest.mark.gpu
 
 TOL_MAX_REL = 1e-2
 TOL_TIGHT = 2e-3
+# Plain-prologue launches run the shared-memory ring kernel by default;
+# NMS_FLAG_REGISTER_RING selects the register-ring kernel.
+KERNELS = {"smem_ring": 0, "register_ring": _lib.NMS_FLAG_REGISTER_RING}
 
 RATIOS = [(2, 4), (4, 8), (8, 16), (16, 32), (32, 64), (64, 128), (128, 256)]
 SHAPES = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]  # out x in (config 2)
@@ -144,7 +147,8 @@ def _seg_args(segs, K, w, w_pad, n, m, x, out, epilogue=_lib.NMS_EPI_STORE):
     return a
 
 
-def test_fused_qkv_three_masks(cuda_device):
+@pytest.mark.parametrize("kernel", sorted(KERNELS))
+def test_fused_qkv_three_masks(cuda_device, kernel):
     """q/k/v with different masks in one launch == three separate products."""
     K, m = 4096, 64
     parts = [make_sparse_device(K, r, m, seed=s, device=cuda_device, std=0.02) for r, s in
@@ -153,6 +157,7 @@ def test_fused_qkv_three_masks(cuda_device):
     x = torch.randn(K, device=cuda_device).to(torch.float16)
     out = torch.empty(6144, device=cuda_device, dtype=torch.float16)
     a = _seg_args([(p[0], p[1]) for p in parts], K, w, parts[0][0].shape[1], nnz, m, x, out)
+    a.flags = KERNELS[kernel]
     _fused(a, cuda_device)
     ref = np.concatenate([_oracle(x, unpack(p[0], w), p[1], K, m) for p in parts])
     _check(out, ref)
@@ -191,7 +196,8 @@ def test_fused_swiglu_with_rmsnorm_prologue(cuda_device):
     assert m_["max_rel"] <= TOL_TIGHT, m_
 
 
-def test_dense_head_argmax(cuda_device):
+@pytest.mark.parametrize("kernel", sorted(KERNELS))
+def test_dense_head_argmax(cuda_device, kernel):
     """Dense output head with greedy argmax epilogue, repeated launches (the
     counter resets itself), ties resolved to the lowest index."""
     V, K = 128256 // 8, 4096
@@ -204,7 +210,7 @@ def test_dense_head_argmax(cuda_device):
     counter = torch.zeros(1, device=cuda_device, dtype=torch.int32)
     tok = torch.full((1,), -1, device=cuda_device, dtype=torch.int64)
     a = _seg_args([(Wd, None)], K, K, K, 1, 1, x, logits, epilogue=_lib.NMS_EPI_ARGMAX)
-    a.flags = _lib.NMS_FLAG_DENSE
+    a.flags = _lib.NMS_FLAG_DENSE | KERNELS[kernel]
     a.amax_val, a.amax_idx = amax_val.data_ptr(), amax_idx.data_ptr()
     a.amax_counter, a.token_out, a.amax_capacity = counter.data_ptr(), tok.data_ptr(), cap
     for _ in range(3):
@@ -260,9 +266,10 @@ def test_nmsparse_linear_module(cuda_device):
 
 
 
-@pytest.mark.parametrize("grid", [0, 1, 37, 148])
+@pytest.mark.parametrize("kernel", sorted(KERNELS))
+@pytest.mark.parametrize("grid", [0, 1, 37, 148, 296])
 @pytest.mark.parametrize("K,h,m", [(4096, 6144, 64), (14336, 4096, 16), (3200, 257, 32), (896, 130, 64)])
-def test_grid_sizes_and_pdl(cuda_device, grid, K, h, m):
+def test_grid_sizes_and_pdl(cuda_device, grid, K, h, m, kernel):
     """Any CTA count (row ranges split unevenly, one CTA doing everything)
     matches the oracle, with and without programmatic dependent launch."""
     packed, mi, w, nnz = make_sparse_device(K, h, m, seed=K * 3 + h, device=cuda_device, std=0.03)
@@ -271,7 +278,72 @@ def test_grid_sizes_and_pdl(cuda_device, grid, K, h, m):
     for pdl in (0, _lib.NMS_FLAG_PDL):
         out = torch.full((h,), float("nan"), device=cuda_device, dtype=torch.float16)
         a = _seg_args([(packed, mi)], K, w, packed.shape[1], nnz, m, x, out)
-        a.flags = pdl
+        a.flags = pdl | KERNELS[kernel]
         a.grid = grid
         _fused(a, cuda_device)
         _check(out, ref)
+
+
+@pytest.mark.parametrize("kernel", sorted(KERNELS))
+def test_fused_swiglu_plain_prologue(cuda_device, kernel):
+    """gate/up with the SwiGLU epilogue on an already-normalised input (plain
+    prologue: the shared-memory ring kernel by default)."""
+    K, I, m = 4096, 14336, 64
+    gate = make_sparse_device(K, I, m, seed=21, device=cuda_device, std=0.02)
+    up = make_sparse_device(K, I, m, seed=22, device=cuda_device, std=0.02)
+    w, nnz = gate[2], gate[3]
+    x = torch.randn(K, device=cuda_device).to(torch.float16)
+    out = torch.empty(I, device=cuda_device, dtype=torch.float16)
+    a = _seg_args([(gate[0], gate[1]), (up[0], up[1])], K, w, gate[0].shape[1], nnz, m, x, out,
+                  epilogue=_lib.NMS_EPI_SWIGLU)
+    a.flags = KERNELS[kernel]
+    _fused(a, cuda_device)
+    g = torch.from_numpy(_oracle(x, unpack(gate[0], w), gate[1], K, m)).to(torch.float16)
+    u = torch.from_numpy(_oracle(x, unpack(up[0], w), up[1], K, m)).to(torch.float16)
+    act = (torch.nn.functional.silu(g.float()).to(torch.float16).float() * u.float()).to(torch.float16)
+    m_ = O.metrics(out.float().cpu().numpy(), act.float().numpy())
+    assert m_["max_rel"] <= TOL_TIGHT, m_
+
+
+@pytest.mark.parametrize("n,m", [(2, 4), (16, 32), (32, 64), (128, 256)])
+def test_ring_kernel_pdl_chain_in_graph(cuda_device, n, m):
+    """Back-to-back dependent launches (each GEMV reads the previous one's
+    output) with programmatic dependent launch in a CUDA graph: the shared-
+    memory ring kernel lets its dependents start at once and fills their
+    rings early, so this checks that every launch still reads its input only
+    after its producer finished.  Each stage against the oracle on the
+    previous stage's fp16 output; replays bit-identical."""
+    K = 4096
+    stages = [make_sparse_device(K, K, m, seed=40 + i, device=cuda_device, std=1.0 / 64) for i in range(6)]
+    w, nnz = stages[0][2], stages[0][3]
+    x0 = torch.randn(K, device=cuda_device).to(torch.float16)
+    bufs = [x0] + [torch.empty(K, device=cuda_device, dtype=torch.float16) for _ in stages]
+    args = []
+    for i, (p, mi, _, _) in enumerate(stages):
+        a = _seg_args([(p, mi)], K, w, p.shape[1], nnz, m, bufs[i], bufs[i + 1])
+        a.flags = _lib.NMS_FLAG_PDL
+        args.append(a)
+    s = torch.cuda.Stream(cuda_device)
+    s.wait_stream(torch.cuda.current_stream(cuda_device))
+    with torch.cuda.stream(s):
+        for a in args:
+            _lib.check(_lib.lib().nms_gemv_fused_f16(ctypes.byref(a), s.cuda_stream))
+    torch.cuda.current_stream(cuda_device).wait_stream(s)
+    torch.cuda.synchronize(cuda_device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for a in args:
+            _lib.check(_lib.lib().nms_gemv_fused_f16(ctypes.byref(a), s.cuda_stream))
+    for b in bufs[1:]:
+        b.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize(cuda_device)
+    first = [b.clone() for b in bufs[1:]]
+    for i, (p, mi, _, _) in enumerate(stages):
+        _check(bufs[i + 1], _oracle(bufs[i], unpack(p, w), mi, K, m))
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(cuda_device)
+    for b, f in zip(bufs[1:], first):
+        assert torch.equal(b, f)
+    assert _lib.device_error() == 0
