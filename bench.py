@@ -504,9 +504,12 @@ def main():
     peaks = measured_peaks()
     achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
     workload = workload_name(args)
-    gemv_roofline = {"bound": "hbm", "kernel": "gemv_packed_kernel", "achieved": round(achieved, 1),
+    # The plan's GEMV launches run the shared-memory ring kernel unless the
+    # L2 look-ahead option sends them to the register-ring kernel.
+    gemv_kernel = "gemv_packed_kernel" if args.prefetch > 0 else "gemv_ring_kernel"
+    gemv_roofline = {"bound": "hbm", "kernel": gemv_kernel, "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "peak_source": peaks["source"], "traffic": profiled_traffic("gemv_packed_kernel", workload),
+                     "peak_source": peaks["source"], "traffic": profiled_traffic(gemv_kernel, workload),
                      "algorithmic_bytes": gemv_bytes, "launches": n_gemv,
                      "mean_launch_us": round(gemv_ms * 1e3 / n_gemv, 3),
                      "note": "the step's GEMV launches alone (plan executor), timed in their own CUDA graph"}

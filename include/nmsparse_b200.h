@@ -153,16 +153,15 @@ int nms_gemm_packed_f16(const void* x, int32_t x_dtype, const void* packed, cons
 #define NMS_PRO_RESID_RMSNORM 1
 #define NMS_FLAG_PDL 1   /* launch with programmatic dependent launch */
 #define NMS_FLAG_DENSE 2 /* dense rows: w == K, mat_index must be NULL */
-/* Plain-prologue launches (no RMSNorm, no prefetch_bytes) run the
- * shared-memory ring kernel: one or two 384-thread CTAs per SM, each at most
- * half an SM; every warp streams its weights through its own ring of 1 KB
- * cp.async slots, filled before the dependency wait, and the CTA lets its
- * dependents launch at once, so with NMS_FLAG_PDL a launch's start-up
- * overlaps the previous launch's stream.  NMS_FLAG_REGISTER_RING selects the
- * register-ring kernel instead (the kernel the RMSNorm prologue and the L2
- * look-ahead always use).  Either kernel reads weights and mask offsets
- * before its dependency wait: they must not be written by the kernel it
- * depends on. */
+/* Launches without prefetch_bytes run the shared-memory ring kernel: one or
+ * two 384-thread CTAs per SM, each at most half an SM; every warp streams its
+ * weights through its own ring of 1 KB cp.async slots, filled before the
+ * dependency wait, and the CTA lets its dependents launch at once, so with
+ * NMS_FLAG_PDL a launch's start-up overlaps the previous launch's stream.
+ * NMS_FLAG_REGISTER_RING selects the register-ring kernel instead (also used
+ * with the L2 look-ahead, and when the rings do not fit).  Either kernel reads
+ * weights, mask offsets and RMSNorm weights before its dependency wait: they
+ * must not be written by the kernel it depends on. */
 #define NMS_FLAG_REGISTER_RING 4
 
 typedef struct nms_segment {

@@ -1,7 +1,8 @@
 // Standalone packed-layout GEMV with per-warp shared-memory weight rings.
 //
-// Same computation as gemv_packed_kernel (plain prologue; store, SwiGLU or
-// argmax epilogue), laid out for back-to-back launches:
+// Same computation as gemv_packed_kernel (plain or residual + RMSNorm
+// prologue; store, SwiGLU or argmax epilogue), laid out for back-to-back
+// launches:
 //
 //   * one CTA per SM, at most half of an SM's registers and shared memory,
 //     so the next launch's CTA fits beside it;
@@ -40,9 +41,10 @@ constexpr int64_t kRingTwoPerSmBytes = 256 * 1024;
 // 16-byte input loads a thread keeps in flight while staging x.
 constexpr int kRingStageLoads = 6;
 
-__host__ __device__ inline size_t gemv_ring_smem_bytes(int D, int K, int w, int w_pad, int nsegx, int max_vrows) {
+__host__ __device__ inline size_t gemv_ring_smem_bytes(int D, int K, int w, int w_pad, int nsegx, int max_vrows,
+                                                       bool norm) {
   size_t off = (size_t)kRingWarps * D * kRingItemBytes;
-  off += align_up_sz((size_t)K * 2, 16);
+  off += align_up_sz((size_t)K * 2, 16) * (norm ? 2 : 1);
   off += align_up_sz((size_t)w, 16) * nsegx;
   off += align_up_sz((size_t)w_pad * 2 * nsegx, 16);
   off += align_up_sz((size_t)max_vrows * 4, 16);
@@ -76,8 +78,11 @@ __global__ void __launch_bounds__(kRingThreads, 2) gemv_ring_kernel(const __grid
   const int max_vrows = (paired ? 2 : 1) * ((p.row_groups + (int)gridDim.x - 1) / (int)gridDim.x) * RG;
   unsigned char* wring = smem_raw + (size_t)warp * D * kRingItemBytes;
   size_t off = (size_t)kRingWarps * D * kRingItemBytes;
+  const bool norm = (p.prologue == kProResidNorm);
   __half* xs = reinterpret_cast<__half*>(smem_raw + off);
   off += align_up_sz((size_t)p.K * 2, 16);
+  __half* nws = reinterpret_cast<__half*>(smem_raw + off);  // RMSNorm weight (norm prologue only)
+  if (norm) off += align_up_sz((size_t)p.K * 2, 16);
   uint8_t* sidx = smem_raw + off;
   off += (size_t)w_al * nsegx;
   __half* xc = reinterpret_cast<__half*>(smem_raw + off);
@@ -120,7 +125,15 @@ __global__ void __launch_bounds__(kRingThreads, 2) gemv_ring_kernel(const __grid
   // their own rings while this CTA streams.
   grid_dep_launch_dependents();
 
-  // --- 2. Mask offsets (weights: independent of the predecessor).
+  // --- 2. Mask offsets and RMSNorm weights (independent of the predecessor).
+  if (norm) {
+    if ((p.K & 7) == 0 && (reinterpret_cast<uintptr_t>(p.norm_w) & 15u) == 0) {
+      for (int i = tid; i < p.K / 8; i += NT)
+        reinterpret_cast<uint4*>(nws)[i] = __ldg(reinterpret_cast<const uint4*>(p.norm_w) + i);
+    } else {
+      for (int i = tid; i < p.K; i += NT) nws[i] = p.norm_w[i];
+    }
+  }
   if (!dense) {
     for (int sx = 0; sx < nsegx; ++sx) {
       const uint8_t* src = p.seg[sx].idx;
@@ -141,26 +154,64 @@ __global__ void __launch_bounds__(kRingThreads, 2) gemv_ring_kernel(const __grid
   //        gather the compressed vector(s) from there.
   grid_dep_wait();
   const __half* xsrc = input_row(p);
-  if ((p.K & 7) == 0 && (reinterpret_cast<uintptr_t>(xsrc) & 15u) == 0) {
+  const bool add = norm && p.x2 != nullptr;
+  float ss = 0.f;
+  if ((p.K & 7) == 0 && (reinterpret_cast<uintptr_t>(xsrc) & 15u) == 0 &&
+      (!add || (reinterpret_cast<uintptr_t>(p.x2) & 15u) == 0)) {
     const int K8 = p.K >> 3;
     const uint4* xv = reinterpret_cast<const uint4*>(xsrc);
+    const uint4* x2v = reinterpret_cast<const uint4*>(p.x2);
     for (int base = tid; base < K8; base += kRingStageLoads * NT) {
-      uint4 a[kRingStageLoads];
+      uint4 a[kRingStageLoads], b[kRingStageLoads];
 #pragma unroll
       for (int u = 0; u < kRingStageLoads; ++u) {
         const int i8 = base + u * NT;
-        a[u] = (i8 < K8) ? __ldcg(xv + i8) : make_uint4(0u, 0u, 0u, 0u);
+        a[u] = b[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (i8 < K8) {
+          a[u] = __ldcg(xv + i8);
+          if (add) b[u] = __ldcg(x2v + i8);
+        }
       }
 #pragma unroll
       for (int u = 0; u < kRingStageLoads; ++u) {
         const int i8 = base + u * NT;
-        if (i8 < K8) reinterpret_cast<uint4*>(xs)[i8] = a[u];
+        if (i8 >= K8) break;
+        if (norm) {
+          // fp16(x + x2) as the reference's residual add rounds it; the
+          // statistic over the rounded values.
+          const __half* ah = reinterpret_cast<const __half*>(&a[u]);
+          const __half* bh = reinterpret_cast<const __half*>(&b[u]);
+          uint4 o;
+          __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const __half hv = add ? f2h(h2f(ah[e]) + h2f(bh[e])) : ah[e];
+            oh[e] = hv;
+            ss = fmaf(h2f(hv), h2f(hv), ss);
+          }
+          a[u] = o;
+        }
+        reinterpret_cast<uint4*>(xs)[i8] = a[u];
       }
     }
   } else {
-    for (int i = tid; i < p.K; i += NT) xs[i] = xsrc[i];
+    for (int i = tid; i < p.K; i += NT) {
+      __half hv = xsrc[i];
+      if (add) hv = f2h(h2f(hv) + h2f(p.x2[i]));
+      xs[i] = hv;
+      ss = fmaf(h2f(hv), h2f(hv), ss);
+    }
   }
-  __syncthreads();
+  float rstd = 1.f;
+  if (norm) {
+    __shared__ float red[kRingWarps];
+    const float tot = block_reduce_sum(ss, red);  // its barriers also publish xs
+    rstd = 1.0f / sqrtf(tot / (float)p.K + p.eps);
+    if (p.resid_out != nullptr && blockIdx.x == 0)
+      for (int i = tid; i < p.K; i += NT) p.resid_out[i] = xs[i];
+  } else {
+    __syncthreads();
+  }
   const int n_shift = ((p.n & (p.n - 1)) == 0) ? __ffs(p.n) - 1 : -1;
   const int wq = p.w_pad >> 2;
   for (int sx = 0; sx < nsegx; ++sx) {
@@ -177,7 +228,10 @@ __global__ void __launch_bounds__(kRingThreads, 2) gemv_ring_kernel(const __grid
         if (j < p.w) {
           const int grp = n_shift >= 0 ? (j >> n_shift) : j / p.n;
           const int col = dense ? j : grp * p.m + (int)((ib >> (8 * e)) & 0xffu);
-          if (col < p.K) val = xs[col];
+          if (col < p.K) {
+            val = xs[col];
+            if (norm) val = f2h(h2f(f2h(h2f(val) * rstd)) * h2f(nws[col]));
+          }
         }
         v[e] = val;
       }

@@ -435,7 +435,7 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
   rec->kind = LaunchRec::kGemvPacked;
   rec->lanes = L;
   rec->ring_depth = 0;
-  if ((a->flags & NMS_FLAG_REGISTER_RING) == 0 && pro == nms::kProPlain && p.pf_items == 0) {
+  if ((a->flags & NMS_FLAG_REGISTER_RING) == 0 && p.pf_items == 0) {
     // One CTA per SM, so that the next launch's CTA fits beside it; two when
     // the stream is long (over 256 KB of weights per SM), where more bytes in
     // flight pay more than the overlap with the neighbouring launches.
@@ -447,7 +447,7 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
     if (rgrid < 1) rgrid = 1;
     const int rvrows = (paired ? 2 : 1) * ((p.row_groups + rgrid - 1) / rgrid) * RG;
     for (int D : {8, 6, 4}) {
-      const size_t rs = nms::gemv_ring_smem_bytes(D, (int)K, (int)w, (int)w_pad, nsegx, rvrows);
+      const size_t rs = nms::gemv_ring_smem_bytes(D, (int)K, (int)w, (int)w_pad, nsegx, rvrows, pro == nms::kProResidNorm);
       if (rs <= nms::kRingSmemCap && rs <= dev->max_smem_optin &&
           !(epi == nms::kEpiArgmax && rgrid > a->amax_capacity)) {
         rec->ring_depth = D;

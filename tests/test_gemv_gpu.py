@@ -23,7 +23,7 @@ pytestmark = pytest.mark.gpu
 
 TOL_MAX_REL = 1e-2
 TOL_TIGHT = 2e-3
-# Plain-prologue launches run the shared-memory ring kernel by default;
+# Launches run the shared-memory ring kernel by default;
 # NMS_FLAG_REGISTER_RING selects the register-ring kernel.
 KERNELS = {"smem_ring": 0, "register_ring": _lib.NMS_FLAG_REGISTER_RING}
 
@@ -163,7 +163,8 @@ def test_fused_qkv_three_masks(cuda_device, kernel):
     _check(out, ref)
 
 
-def test_fused_swiglu_with_rmsnorm_prologue(cuda_device):
+@pytest.mark.parametrize("kernel", sorted(KERNELS))
+def test_fused_swiglu_with_rmsnorm_prologue(cuda_device, kernel):
     """gate/up launch with the residual-add + RMSNorm prologue and the SwiGLU
     epilogue, against the fp16-rounding sequence of model.py:185-188, 255-270."""
     K, I, m = 4096, 14336, 64
@@ -182,6 +183,7 @@ def test_fused_swiglu_with_rmsnorm_prologue(cuda_device):
     a.norm_weight = nw.data_ptr()
     a.eps = 1e-5
     a.resid_out = resid.data_ptr()
+    a.flags = KERNELS[kernel]
     _fused(a, cuda_device)
     # host restatement of the reference's roundings
     h = (xa.float() + xb.float()).to(torch.float16)
