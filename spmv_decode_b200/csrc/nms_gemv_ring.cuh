@@ -8,7 +8,8 @@
 //     so the next launch's CTA fits beside it;
 //   * every warp streams its weight items through its own ring of D 1 KB
 //     slots with 16-byte cp.async copies (no registers held per byte in
-//     flight: D = 8 keeps 96 KB per SM in flight at 12 warps);
+//     flight: D = 8 keeps 96 KB per SM in flight at 12 warps; the deepest
+//     ring of D = 8..4 that fits is used);
 //   * the ring is filled and the mask offsets are staged BEFORE the
 //     programmatic-dependency wait (weights never depend on an earlier
 //     kernel), and the CTA lets its dependents launch at once.
@@ -51,7 +52,9 @@ __host__ __device__ inline size_t gemv_ring_smem_bytes(int D, int K, int w, int 
   return off;
 }
 
-template <int L, int D>
+// NORM: the residual + RMSNorm prologue (a compile-time switch, so the plain
+// launches keep the lean staging loop).
+template <int L, int D, bool NORM>
 __global__ void __launch_bounds__(kRingThreads, 2) gemv_ring_kernel(const __grid_constant__ GemvParams p) {
   constexpr int RG = kWarp / L, NT = kRingThreads, CB = 32 * L;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -78,7 +81,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) gemv_ring_kernel(const __grid
   const int max_vrows = (paired ? 2 : 1) * ((p.row_groups + (int)gridDim.x - 1) / (int)gridDim.x) * RG;
   unsigned char* wring = smem_raw + (size_t)warp * D * kRingItemBytes;
   size_t off = (size_t)kRingWarps * D * kRingItemBytes;
-  const bool norm = (p.prologue == kProResidNorm);
+  constexpr bool norm = NORM;
   __half* xs = reinterpret_cast<__half*>(smem_raw + off);
   off += align_up_sz((size_t)p.K * 2, 16);
   __half* nws = reinterpret_cast<__half*>(smem_raw + off);  // RMSNorm weight (norm prologue only)

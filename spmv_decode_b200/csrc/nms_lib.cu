@@ -69,6 +69,13 @@ struct DeviceInfo {
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
 
+// The ring GEMV instantiations of one ring depth (every lanes-per-row
+// variant, both prologues).
+#define NMS_RING_KERNELS_N(D, N)                                                                    \
+  (const void*)nms::gemv_ring_kernel<32, D, N>, (const void*)nms::gemv_ring_kernel<16, D, N>,     \
+      (const void*)nms::gemv_ring_kernel<8, D, N>, (const void*)nms::gemv_ring_kernel<4, D, N>
+#define NMS_RING_KERNELS(D) NMS_RING_KERNELS_N(D, false), NMS_RING_KERNELS_N(D, true)
+
 // Per-device one-time setup: SM count, opt-in shared memory, and the
 // function attributes of every kernel instantiation.
 int device_info(const DeviceInfo** out) {
@@ -93,12 +100,7 @@ int device_info(const DeviceInfo** out) {
         (const void*)nms::gemv_packed_kernel<32>, (const void*)nms::gemv_packed_kernel<16>,
         (const void*)nms::gemv_packed_kernel<8>,  (const void*)nms::gemv_packed_kernel<4>,
         (const void*)nms::gemv_ref_kernel<8, false>, (const void*)nms::gemv_ref_kernel<8, true>,
-        (const void*)nms::gemv_ring_kernel<32, 8>, (const void*)nms::gemv_ring_kernel<16, 8>,
-        (const void*)nms::gemv_ring_kernel<8, 8>,  (const void*)nms::gemv_ring_kernel<4, 8>,
-        (const void*)nms::gemv_ring_kernel<32, 6>, (const void*)nms::gemv_ring_kernel<16, 6>,
-        (const void*)nms::gemv_ring_kernel<8, 6>,  (const void*)nms::gemv_ring_kernel<4, 6>,
-        (const void*)nms::gemv_ring_kernel<32, 4>, (const void*)nms::gemv_ring_kernel<16, 4>,
-        (const void*)nms::gemv_ring_kernel<8, 4>,  (const void*)nms::gemv_ring_kernel<4, 4>,
+        NMS_RING_KERNELS(8), NMS_RING_KERNELS(6), NMS_RING_KERNELS(5), NMS_RING_KERNELS(4),
     };
     size_t static_max = 0;
     for (const void* k : dyn_smem_kernels) {
@@ -112,12 +114,7 @@ int device_info(const DeviceInfo** out) {
     // The ring GEMV keeps its CTA at most half an SM so that the next
     // launch's CTA fits beside it: ask for the largest shared-memory carveout
     // (the default sizes the carveout for one CTA's need).
-    for (const void* k : {(const void*)nms::gemv_ring_kernel<32, 8>, (const void*)nms::gemv_ring_kernel<16, 8>,
-                          (const void*)nms::gemv_ring_kernel<8, 8>, (const void*)nms::gemv_ring_kernel<4, 8>,
-                          (const void*)nms::gemv_ring_kernel<32, 6>, (const void*)nms::gemv_ring_kernel<16, 6>,
-                          (const void*)nms::gemv_ring_kernel<8, 6>, (const void*)nms::gemv_ring_kernel<4, 6>,
-                          (const void*)nms::gemv_ring_kernel<32, 4>, (const void*)nms::gemv_ring_kernel<16, 4>,
-                          (const void*)nms::gemv_ring_kernel<8, 4>, (const void*)nms::gemv_ring_kernel<4, 4>}) {
+    for (const void* k : {NMS_RING_KERNELS(8), NMS_RING_KERNELS(6), NMS_RING_KERNELS(5), NMS_RING_KERNELS(4)}) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
       if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(PreferredSharedMemoryCarveout)");
     }
@@ -220,19 +217,28 @@ struct LaunchRec {
   bool pdl = false;
 };
 
-template <int D>
+template <int D, bool NORM>
 cudaError_t launch_gemv_ring_d(const LaunchRec& r, cudaStream_t st) {
   switch (r.lanes) {
-    case 32: return launch_ex(nms::gemv_ring_kernel<32, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
-    case 16: return launch_ex(nms::gemv_ring_kernel<16, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
-    case 8: return launch_ex(nms::gemv_ring_kernel<8, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
-    default: return launch_ex(nms::gemv_ring_kernel<4, D>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+    case 32: return launch_ex(nms::gemv_ring_kernel<32, D, NORM>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+    case 16: return launch_ex(nms::gemv_ring_kernel<16, D, NORM>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+    case 8: return launch_ex(nms::gemv_ring_kernel<8, D, NORM>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+    default: return launch_ex(nms::gemv_ring_kernel<4, D, NORM>, r.grid, r.block, r.smem, st, r.pdl, r.cluster, r.gp);
+  }
+}
+
+template <bool NORM>
+cudaError_t launch_gemv_ring_n(const LaunchRec& r, cudaStream_t st) {
+  switch (r.ring_depth) {
+    case 8: return launch_gemv_ring_d<8, NORM>(r, st);
+    case 6: return launch_gemv_ring_d<6, NORM>(r, st);
+    case 5: return launch_gemv_ring_d<5, NORM>(r, st);
+    default: return launch_gemv_ring_d<4, NORM>(r, st);
   }
 }
 
 cudaError_t launch_gemv_ring(const LaunchRec& r, cudaStream_t st) {
-  return r.ring_depth >= 8 ? launch_gemv_ring_d<8>(r, st)
-                           : (r.ring_depth >= 6 ? launch_gemv_ring_d<6>(r, st) : launch_gemv_ring_d<4>(r, st));
+  return r.gp.prologue == nms::kProResidNorm ? launch_gemv_ring_n<true>(r, st) : launch_gemv_ring_n<false>(r, st);
 }
 
 int launch_rec(const LaunchRec& r, cudaStream_t st) {
@@ -446,7 +452,7 @@ int prepare_gemv(const nms_gemv_fused_args* a, LaunchRec* rec) {
     if (rgrid > p.row_groups) rgrid = p.row_groups;
     if (rgrid < 1) rgrid = 1;
     const int rvrows = (paired ? 2 : 1) * ((p.row_groups + rgrid - 1) / rgrid) * RG;
-    for (int D : {8, 6, 4}) {
+    for (int D : {8, 6, 5, 4}) {
       const size_t rs = nms::gemv_ring_smem_bytes(D, (int)K, (int)w, (int)w_pad, nsegx, rvrows, pro == nms::kProResidNorm);
       if (rs <= nms::kRingSmemCap && rs <= dev->max_smem_optin &&
           !(epi == nms::kEpiArgmax && rgrid > a->amax_capacity)) {
