@@ -41,6 +41,20 @@ ARGMAX_CAPACITY = 2048
 # Persistent kernels tried before the barrier kernel in modes "auto" and
 # "persistent" (the dataflow kernel, when enabled).
 FLOW_DEFAULT: List[str] = []
+# Mode "auto": below this many GEMV weight bytes per layer the plan executor
+# (one launch per kernel, programmatic dependent launch) is faster than the
+# persistent step, whose fixed cost per stage boundary dominates small
+# layers.  Measured on one B200 (ms/token, persistent / plan): Qwen3-0.6B
+# 32:64 (16 MB per layer) 1.136 / 0.842; Llama-3.1-8B 32:64 (218 MB)
+# 2.183 / 2.116 with host I/O every step 2.215 / 2.225; Qwen3-32B 16:32
+# (488 MB) 7.151 / 7.783.
+AUTO_PLAN_BELOW_LAYER_BYTES = 64 << 20
+
+
+def auto_executor(layer_gemv_bytes: float) -> str:
+    """The executor mode "auto" picks for a model with this many GEMV
+    weight bytes per decoder layer: "plan" or "persistent"."""
+    return "plan" if layer_gemv_bytes < AUTO_PLAN_BELOW_LAYER_BYTES else "persistent"
 
 # Device error codes (include/nmsparse_b200.h, nms_device_error).
 DEVICE_ERRORS = {
@@ -151,6 +165,9 @@ class DecodeEngine:
             self._build(model, attn_splits)
             self._steps = {}
             self.mode = "plan"
+            layer_bytes = sum(r["bytes"] for r in self.gemv_records if not r["argmax"]) / max(1, c.n_layer)
+            if mode == "auto" and auto_executor(layer_bytes) == "plan":
+                mode = "plan"
             if mode != "plan" and allreduce is None and head_hook is None:
                 # Persistent executors, in order of preference: the dataflow
                 # kernel (no grid barriers), then the barrier kernel.

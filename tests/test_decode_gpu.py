@@ -229,13 +229,17 @@ def test_dense_linears_engine(cuda_device, mode):
 
 
 
-def test_auto_mode_is_persistent(cuda_device):
+def test_mixed_lane_widths_run_persistent(cuda_device):
     """Mixed packed widths (lanes per row 8 and 16 in one step) run in the
-    persistent kernel."""
+    persistent kernel; mode "auto" picks the plan executor for layers this
+    small."""
     model = build_model(ModelArgs(block_size=64, vocab_size=512, n_layer=1, n_head=2, n_local_heads=1, dim=256,
                                   intermediate_size=384), nm=(16, 32), device=cuda_device, seed=5)
-    eng = DecodeEngine(model, 32, history_len=32, mode="auto")
+    eng = DecodeEngine(model, 32, history_len=32, mode="persistent")
     assert eng.mode == "persistent"
+    eng.close()
+    eng = DecodeEngine(model, 32, history_len=32, mode="auto")
+    assert eng.mode == "plan"
     eng.close()
 
 
