@@ -615,9 +615,11 @@ def main():
         from oracle.decode_oracle import cpu_decode_sample
 
         r = cpu_decode_sample(cfg, nm, args.ctx, sample_layers=args.cpu_layers, steps=3,
-                              threads=os.cpu_count(), seed=args.seed, warmup=3)
+                              threads=os.cpu_count(), seed=args.seed, warmup=3, single_thread_steps=1)
         cpu = {"value": round(r["ms_per_token"], 3), "unit": UNIT, "cores": r["threads"], "kind": "port",
-               "sample": r["sample"]}
+               "sample": r["sample"],
+               # the same sample on one host thread (torch.set_num_threads(1)), one timed step
+               "single_thread": {"value": round(r["single_thread_ms_per_token"], 3), "unit": UNIT, "cores": 1}}
 
     if rank == 0:
         pub = PUBLISHED.get((args.model, args.nm))

@@ -297,13 +297,16 @@ def _masked_random(rows: int, K: int, m: Optional[int], std: float, gen: torch.G
 
 
 def cpu_decode_sample(config, nm: Optional[tuple], ctx: int, sample_layers: int = 2, steps: int = 3,
-                      threads: Optional[int] = None, seed: int = 0, warmup: int = 1) -> dict:
+                      threads: Optional[int] = None, seed: int = 0, warmup: int = 1,
+                      single_thread_steps: int = 0) -> dict:
     """Time the reference's torch CPU decode path on a bounded sample of a
     workload: ``sample_layers`` decoder layers of the configuration's shapes
     plus the full output head, dense masked fp16 weights multiplied with
     F.linear (the reference's CPU path, microbench_triton_torchmv.py:210-211),
     KV cache ~ N(0, 0.02) of length ``ctx``.  The per-token time of the whole
-    model is extrapolated as n_layer * (layer time) + head time."""
+    model is extrapolated as n_layer * (layer time) + head time.
+    ``single_thread_steps`` > 0 also times that many steps of the same sample
+    on one host thread (``single_thread_ms_per_token``)."""
     import time
 
     if threads:
@@ -335,23 +338,37 @@ def cpu_decode_sample(config, nm: Optional[tuple], ctx: int, sample_layers: int 
     for _ in range(max(1, warmup)):  # untimed warm-up steps
         om.step(123, ctx)
         om._linear(om.head, x)
-    t_step, t_head = [], []
-    for i in range(steps):
-        t0 = time.perf_counter()
-        om.step(123, ctx)
-        t1 = time.perf_counter()
-        om._linear(om.head, x)
-        t2 = time.perf_counter()
-        t_step.append(t1 - t0)
-        t_head.append(t2 - t1)
-    step_s = sorted(t_step)[len(t_step) // 2]
-    head_s = sorted(t_head)[len(t_head) // 2]
-    layer_s = max(step_s - head_s, 0.0) / sample_layers
+    def timed(n):
+        t_step, t_head = [], []
+        for i in range(n):
+            t0 = time.perf_counter()
+            om.step(123, ctx)
+            t1 = time.perf_counter()
+            om._linear(om.head, x)
+            t2 = time.perf_counter()
+            t_step.append(t1 - t0)
+            t_head.append(t2 - t1)
+        step_s = sorted(t_step)[len(t_step) // 2]
+        head_s = sorted(t_head)[len(t_head) // 2]
+        return max(step_s - head_s, 0.0) / sample_layers, head_s
+
+    layer_s, head_s = timed(steps)
+    used = torch.get_num_threads()
+    single = None
+    if single_thread_steps > 0:
+        torch.set_num_threads(1)
+        try:
+            om.step(123, ctx)  # one untimed step on the single thread
+            l1, h1 = timed(single_thread_steps)
+            single = 1e3 * (c.n_layer * l1 + h1)
+        finally:
+            torch.set_num_threads(used)
     return {
         "ms_per_token": 1e3 * (c.n_layer * layer_s + head_s),
+        "single_thread_ms_per_token": single,
         "layer_ms": 1e3 * layer_s,
         "head_ms": 1e3 * head_s,
-        "threads": torch.get_num_threads(),
+        "threads": used,
         "sample": f"{sample_layers} of {c.n_layer} decoder layers + full output head, ctx {ctx}, "
                   f"median of {steps} steps, dense masked fp16 F.linear; per-token time = "
                   f"{c.n_layer} x layer + head",
