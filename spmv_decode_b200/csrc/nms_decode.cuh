@@ -19,7 +19,7 @@
 
 namespace nms {
 
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 512;  // one (head, position) score and one (head, dim) output per thread at GQA 8
 constexpr int kAttnD = 128;       // head_dim supported by this kernel
 constexpr int kAttnMaxGroup = 8;  // q heads per KV head (one warp each)
 constexpr int kAttnTile = 64;     // positions per tile (two per lane in the softmax)
@@ -249,12 +249,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const __
       }
     }
     __syncthreads();
-    // (d) P*V: (head, dim) pairs spread over the CTA.
+    // (d) P*V: (head, dim) pairs spread over the CTA; four independent FMA
+    //     chains over the tile's positions (a single chain made this loop,
+    //     not the loads, grow the kernel with the context).
     for (int i = tid; i < G * D; i += NT) {
       const int g = i / D, d = i - g * D;
-      float acc = so[g][d] * scorr[g];
-      for (int r = 0; r < nt; ++r) acc = fmaf(sp[g][r], h2f(sv[r][d]), acc);
-      so[g][d] = acc;
+      float a0 = so[g][d] * scorr[g], a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      int r = 0;
+      for (; r + 3 < nt; r += 4) {
+        a0 = fmaf(sp[g][r], h2f(sv[r][d]), a0);
+        a1 = fmaf(sp[g][r + 1], h2f(sv[r + 1][d]), a1);
+        a2 = fmaf(sp[g][r + 2], h2f(sv[r + 2][d]), a2);
+        a3 = fmaf(sp[g][r + 3], h2f(sv[r + 3][d]), a3);
+      }
+      for (; r < nt; ++r) a0 = fmaf(sp[g][r], h2f(sv[r][d]), a0);
+      so[g][d] = (a0 + a1) + (a2 + a3);
     }
     __syncthreads();
   }

@@ -43,12 +43,13 @@ ARGMAX_CAPACITY = 2048
 FLOW_DEFAULT: List[str] = []
 # Mode "auto": below this many GEMV weight bytes per layer the plan executor
 # (one launch per kernel, programmatic dependent launch) is faster than the
-# persistent step, whose fixed cost per stage boundary dominates small
-# layers.  Measured on one B200 (ms/token, persistent / plan): Qwen3-0.6B
-# 32:64 (16 MB per layer) 1.136 / 0.842; Llama-3.1-8B 32:64 (218 MB)
-# 2.183 / 2.116 with host I/O every step 2.215 / 2.225; Qwen3-32B 16:32
-# (488 MB) 7.151 / 7.783.
-AUTO_PLAN_BELOW_LAYER_BYTES = 64 << 20
+# persistent step, whose fixed cost per stage boundary weighs more the
+# smaller the layer.  Measured on one B200 (ms/token, persistent / plan; CUDA
+# graph replay, then with host I/O every step): Qwen3-0.6B 32:64 (16 MB per
+# layer) 1.136 / 0.830, 1.166 / 0.885; Llama-3.1-8B 32:64 (218 MB)
+# 2.181 / 2.106, 2.214 / 2.176; Qwen3-32B 16:32 (488 MB) 7.187 / 7.716,
+# 7.261 / 7.835.
+AUTO_PLAN_BELOW_LAYER_BYTES = 320 << 20
 
 
 def auto_executor(layer_gemv_bytes: float) -> str:

@@ -68,12 +68,12 @@ def test_check_device_names_every_code(monkeypatch):
 
 def test_auto_executor_by_layer_bytes():
     """Mode "auto" runs small layers on the plan executor and large ones on
-    the persistent step (the measured crossover sits between Qwen3-0.6B's
-    16 MB and Llama-3.1-8B's 218 MB of GEMV weights per layer)."""
+    the persistent step (the measured crossover sits between Llama-3.1-8B's
+    218 MB and Qwen3-32B's 488 MB of GEMV weights per layer)."""
     from spmv_decode_b200.engine import AUTO_PLAN_BELOW_LAYER_BYTES, auto_executor
 
     assert auto_executor(15.7e6) == "plan"
-    assert auto_executor(218e6) == "persistent"
+    assert auto_executor(218e6) == "plan"
     assert auto_executor(488e6) == "persistent"
     assert auto_executor(AUTO_PLAN_BELOW_LAYER_BYTES - 1) == "plan"
     assert auto_executor(AUTO_PLAN_BELOW_LAYER_BYTES) == "persistent"
